@@ -1,0 +1,417 @@
+"""Benchmark of the INT4 paged KV-cache hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (Llama-3-8B shape): 64 sequences x 4096 tokens
+of INT4 paged cache (Hq=32, Hkv=8, D=128, page 16, group 32, pages scattered
+by a random permutation over a pool of 64 x 257 pages; K/V ~N(0,1) fp16 with
+4 outlier K channels x8, written by the fused append), then per step
+
+    decode attention over the 4096 cached tokens of every sequence, and
+    a batched 1-token fused RoPE+INT4 append per sequence at position 4096.
+
+One process per GPU (torchrun for N > 1): every rank owns an independent
+copy of the workload (sequences are partitioned across GPUs, no collective),
+so ``scaling`` is "weak" and ``value`` is the aggregate over ranks.
+
+``value``: algorithmic bytes of the step (decode + append) x N /
+max-over-ranks step time, in TB/s, with inputs resident in HBM; the step is
+replayed from a CUDA graph (validation in deferred mode, no host syncs).
+``e2e``: the same metric through the public Python API with host buffers:
+per step the new query / K / V / positions / slots are copied from pinned
+host memory, the reference-semantics (synchronous validation) calls run,
+and the fp16 output is copied back.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "iris-kernel_b200"))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+B, L, HQ, HKV, D, P, G = 64, 4096, 32, 8, 128, 16, 32
+POOL = B * (L // P + 1)
+OUTLIER_CH = (3, 40, 77, 121)
+
+# algorithmic bytes (DESIGN.md "Measurement"): KV pages + scales read once,
+# Q read, O written, block table read; append reads K, V (fp16) and writes
+# packed bytes + scales, plus slots/positions and one cos/sin row.
+DECODE_BYTES = B * L * HKV * (D + D // 8) + 2 * B * HQ * D * 2 + B * (L // P + 1) * 4
+APPEND_BYTES = B * HKV * (4 * D + D + D // 8) + B * 8 + 2 * (D // 2) * 2
+STEP_BYTES = DECODE_BYTES + APPEND_BYTES
+SPEC_TBS = 8.0
+
+
+def _peak_gbs():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            v = float(json.load(f)["hbm_gbs"])
+        return v, "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def _dist():
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+        return dist, dist.get_rank(), dist.get_world_size(), local
+    return None, 0, 1, 0
+
+
+class Clocks:
+    """Samples SM clocks and throttle reasons with nvidia-smi while running."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{index}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "power_w_max": max(r[2] for r in rows), "samples": len(rows), "reasons": reasons}
+
+
+def build_workload(dev, seed):
+    """Cache written by the fused append from synthetic K/V (config 2)."""
+    from iris_kernel.fused_kv import fused_rope_int4_paged_append
+    from oracle import iris_oracle as orc  # RoPE table builder only (host arrays)
+
+    g = torch.Generator(device=dev).manual_seed(seed)
+    perm = torch.randperm(POOL, generator=g, device=dev).int()
+    bt = perm.view(B, L // P + 1).contiguous()
+    kd = torch.zeros(POOL, P, HKV, D // 2, dtype=torch.uint8, device=dev)
+    vd = torch.zeros_like(kd)
+    ks = torch.zeros(POOL, P, HKV, D // G, dtype=torch.float16, device=dev)
+    vs = torch.zeros_like(ks)
+    cos_np, sin_np = orc.rope_cache(L + 1, D)
+    cos, sin = torch.from_numpy(cos_np).to(dev), torch.from_numpy(sin_np).to(dev)
+    pos = torch.arange(L, device=dev, dtype=torch.int32)
+    for b in range(B):
+        k = torch.randn(L, HKV, D, generator=g, device=dev)
+        k[..., list(OUTLIER_CH)] *= 8
+        v = torch.randn(L, HKV, D, generator=g, device=dev)
+        slots = (bt[b, (pos // P).long()] * P + pos % P).int()
+        fused_rope_int4_paged_append(k.half(), v.half(), pos, slots, cos, sin, kd, vd, ks, vs, rotary_dim=D,
+                                     page_size=P)
+    q = torch.randn(B, HQ, D, generator=g, device=dev).half()
+    knew = torch.randn(B, HKV, D, generator=g, device=dev)
+    knew[..., list(OUTLIER_CH)] *= 8
+    vnew = torch.randn(B, HKV, D, generator=g, device=dev)
+    w = dict(q=q, kd=kd, vd=vd, ks=ks, vs=vs, bt=bt, cos=cos, sin=sin,
+             lens=torch.full((B,), L, dtype=torch.int32, device=dev),
+             knew=knew.half(), vnew=vnew.half(), newpos=torch.full((B,), L, dtype=torch.int32, device=dev),
+             newslot=(bt[:, L // P] * P).int().contiguous(), out=torch.empty(B, HQ, D, dtype=torch.float16,
+                                                                             device=dev))
+    torch.cuda.synchronize(dev)
+    return w
+
+
+def step_decode(w):
+    from iris_kernel.fused_attention import fused_int4_paged_decode_attention
+
+    fused_int4_paged_decode_attention(w["q"], w["kd"], w["vd"], w["ks"], w["vs"], w["bt"], w["lens"], w["out"])
+
+
+def step_append(w):
+    from iris_kernel.fused_kv import fused_rope_int4_paged_append
+
+    fused_rope_int4_paged_append(w["knew"], w["vnew"], w["newpos"], w["newslot"], w["cos"], w["sin"], w["kd"],
+                                 w["vd"], w["ks"], w["vs"], rotary_dim=D, page_size=P)
+
+
+def graph_of(fn, dev):
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            fn()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    torch.cuda.synchronize(dev)
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        fn()
+    torch.cuda.synchronize(dev)
+    return gr
+
+
+def timed(fn, steps, dev, dist, warmup):
+    """Warm up, barrier + sync, time exactly `steps` calls with CUDA events
+    on the current stream, barrier + sync; returns ms for all steps."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.record()
+    for _ in range(steps):
+        fn()
+    en.record()
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    return st.elapsed_time(en)
+
+
+def max_over_ranks(x, dist, dev):
+    if dist is None:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_baseline_sample(seconds_budget=15.0):
+    """The CPU oracle (numpy port of the reference's eager path) on a bounded
+    sample of the same workload: decode of whole 4096-token sequences plus the
+    64-token append, repeated until the budget is used.  Returns TB/s of
+    algorithmic bytes and a description."""
+    from oracle import iris_oracle as orc
+
+    rng = np.random.default_rng(0)
+    nseq = 4
+    NPs = nseq * (L // P)
+    kd = rng.integers(0, 256, (NPs, P, HKV, D // 2), dtype=np.uint8)
+    vd = rng.integers(0, 256, (NPs, P, HKV, D // 2), dtype=np.uint8)
+    ks = rng.uniform(0.01, 1, (NPs, P, HKV, D // G)).astype(np.float16)
+    vs = rng.uniform(0.01, 1, (NPs, P, HKV, D // G)).astype(np.float16)
+    bt = rng.permutation(NPs).astype(np.int32).reshape(nseq, L // P)
+    lens = np.full(nseq, L, np.int32)
+    q = rng.standard_normal((nseq, HQ, D)).astype(np.float16)
+    cos, sin = orc.rope_cache(L + 1, D)
+    knew = rng.standard_normal((B, HKV, D)).astype(np.float16)
+    vnew = rng.standard_normal((B, HKV, D)).astype(np.float16)
+    apool = B
+    akd = np.zeros((apool, P, HKV, D // 2), np.uint8)
+    avd, aks, avs = akd.copy(), np.zeros((apool, P, HKV, D // G), np.float16), None
+    avs = aks.copy()
+    done_bytes = 0
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        orc.decode_attention(q, kd, vd, ks, vs, bt, lens)
+        orc.append(knew, vnew, np.full(B, L, np.int32), (np.arange(B) * P).astype(np.int32), cos, sin, akd, avd, aks,
+                   avs, rotary_dim=D, group_size=G, page_size=P)
+        reps += 1
+        done_bytes += nseq * L * HKV * (D + D // 8) + 2 * nseq * HQ * D * 2 + nseq * (L // P) * 4 + APPEND_BYTES
+        if time.perf_counter() - t0 > seconds_budget:
+            break
+    dt = time.perf_counter() - t0
+    return done_bytes / dt / 1e12, (f"{reps} x (decode of {nseq} of the 64 sequences x 4096 tokens + the 64-token "
+                                    f"append), numpy oracle, {dt:.1f} s"), dt
+
+
+def run_reference(args, dist, rank, world):
+    """The reference's CPU path (numpy port of its eager code; the reference
+    itself does not travel to the GPU box) on host cores, rank 0 only."""
+    if rank != 0:
+        return
+    budget = max(2.0, 60.0 / max(1, args.steps + args.warmup))
+    for _ in range(args.warmup):
+        cpu_baseline_sample(seconds_budget=0.1)
+    vals = []
+    desc = ""
+    for _ in range(args.steps):
+        v, desc, _ = cpu_baseline_sample(seconds_budget=budget)
+        vals.append(v)
+    value = statistics.median(vals)
+    cores = os.cpu_count()
+    line = {
+        "impl": "reference", "metric": "decode-attn achieved HBM TB/s (% of B200 peak) + us/step; append tokens/s",
+        "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": STEP_BYTES / (value * 1e12) * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp16/int4->fp32", "data": "synthetic",
+        "config": _config(),
+        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": cores, "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _config():
+    return {"workload": "BASELINE config 2: Llama-3-8B-shaped INT4 paged decode 64 x 4096 + 1-token append",
+            "batch": B, "context": L, "hq": HQ, "hkv": HKV, "head_dim": D, "page_size": P, "group": G,
+            "pool_pages": POOL, "l2": "no flush: each step reads 303 MB of cache > 126 MB L2",
+            "parallelism": "sequence-sharded replicas (one 64x4096 batch per GPU)",
+            "validation": "deferred (value), synchronous (e2e)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    dist, rank, world, local = _dist()
+    if args.impl == "reference":
+        run_reference(args, dist, rank, world)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+
+    import iris_kernel
+    from iris_kernel.fused_attention import fused_int4_paged_decode_attention
+    from iris_kernel.fused_kv import fused_rope_int4_paged_append
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    w = build_workload(dev, seed=1234 + rank)
+
+    # ---- value: graph-replayed steps, inputs resident ----
+    iris_kernel.set_validation_mode("deferred")
+    g_step = graph_of(lambda: (step_decode(w), step_append(w)), dev)
+    g_dec = graph_of(lambda: step_decode(w), dev)
+    g_app = graph_of(lambda: step_append(w), dev)
+    with Clocks(local) as clk:
+        ms = timed(g_step.replay, args.steps, dev, dist, args.warmup)
+        ms_dec = timed(g_dec.replay, args.steps, dev, dist, args.warmup)
+        ms_app = timed(g_app.replay, args.steps, dev, dist, args.warmup)
+    iris_kernel.check_errors(dev)
+    iris_kernel.set_validation_mode("sync")
+    ms = max_over_ranks(ms, dist, dev)
+    ms_dec = max_over_ranks(ms_dec, dist, dev)
+    ms_app = max_over_ranks(ms_app, dist, dev)
+    step_ms = ms / args.steps
+    dec_us = ms_dec / args.steps * 1e3
+    app_us = ms_app / args.steps * 1e3
+    value = world * STEP_BYTES / (step_ms * 1e-3) / 1e12
+
+    # ---- e2e: public API with host buffers ----
+    hq = torch.empty_like(w["q"], device="cpu").pin_memory()
+    hk = torch.empty_like(w["knew"], device="cpu").pin_memory()
+    hv = torch.empty_like(w["vnew"], device="cpu").pin_memory()
+    hp = torch.empty_like(w["newpos"], device="cpu").pin_memory()
+    hs = torch.empty_like(w["newslot"], device="cpu").pin_memory()
+    hout = torch.empty_like(w["out"], device="cpu").pin_memory()
+    hq.copy_(w["q"])
+    hk.copy_(w["knew"])
+    hv.copy_(w["vnew"])
+    hp.copy_(w["newpos"])
+    hs.copy_(w["newslot"])
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hp, hs))
+    d2h = hout.numel() * hout.element_size()
+
+    def e2e_step():
+        q = hq.to(dev, non_blocking=True)
+        k = hk.to(dev, non_blocking=True)
+        v = hv.to(dev, non_blocking=True)
+        p = hp.to(dev, non_blocking=True)
+        s = hs.to(dev, non_blocking=True)
+        out = fused_int4_paged_decode_attention(q, w["kd"], w["vd"], w["ks"], w["vs"], w["bt"], w["lens"])
+        fused_rope_int4_paged_append(k, v, p, s, w["cos"], w["sin"], w["kd"], w["vd"], w["ks"], w["vs"],
+                                     rotary_dim=D, page_size=P)
+        hout.copy_(out, non_blocking=True)
+
+    ms_e2e = timed(e2e_step, args.steps, dev, dist, args.warmup)
+    ms_e2e = max_over_ranks(ms_e2e, dist, dev)
+    e2e_value = world * STEP_BYTES / (ms_e2e / args.steps * 1e-3) / 1e12
+
+    clocks = clk.summary()
+    peak, peak_kind = _peak_gbs()
+    achieved = DECODE_BYTES / (dec_us * 1e-6) / 1e9
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "decode_c2_traffic.json")
+    if os.path.exists(tpath):
+        try:
+            traffic = json.load(open(tpath)).get("dram_bytes_per_launch")
+        except Exception:
+            traffic = None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, desc, _ = cpu_baseline_sample(seconds_budget=15.0)
+        cpu = {"value": v, "unit": "TB/s", "cores": os.cpu_count(), "kind": "port", "sample": desc}
+
+    if rank == 0:
+        line = {
+            "metric": "decode-attn achieved HBM TB/s (% of B200 peak) + us/step; append tokens/s",
+            "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp16/int4->fp32", "data": "synthetic (seeded N(0,1), random page permutation)",
+            "config": _config(),
+            "us_per_step": step_ms * 1e3,
+            "decode_us": dec_us, "decode_tbs": DECODE_BYTES / (dec_us * 1e-6) / 1e12,
+            "decode_pct_of_8tbs": 100 * DECODE_BYTES / (dec_us * 1e-6) / 1e12 / SPEC_TBS,
+            "decode_pct_of_measured": 100 * achieved / peak,
+            "append_us": app_us, "append_tokens_per_s": world * B / (app_us * 1e-6),
+            "step_bytes": STEP_BYTES, "decode_bytes": DECODE_BYTES, "append_bytes": APPEND_BYTES,
+            "e2e": {"value": e2e_value, "unit": "TB/s", "ms_per_step": ms_e2e / args.steps,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": 5 * args.steps,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": peak_kind, "traffic": traffic,
+                         "kernel": "decode (plan + decode + combine launches) timed alone from a CUDA graph"},
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    del g_step, g_dec, g_app
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,164 @@
+/*
+ * iris_b200.h -- C ABI of the B200-native (sm_100a) INT4 paged KV-cache kernels.
+ *
+ * Drop-in replacement for the two device hot paths of Hunter2030ZeRo/Iris-Kernel:
+ *
+ *   write: src/iris_kernel/fused_kv.py:419-597 (_rope_int4_paged_append kernel,
+ *          launched by fused_rope_int4_paged_append, fused_kv.py:600-780)
+ *   read:  src/iris_kernel/fused_attention.py:11-220 (_int4_paged_decode_attention
+ *          kernel, launched by fused_int4_paged_decode_attention, :437-525)
+ *
+ * All pointers are device pointers unless stated otherwise; tensors are
+ * dense row-major (C-contiguous).  `stream` is a cudaStream_t (NULL = legacy
+ * default stream).  Every call is asynchronous on `stream`; the return value
+ * reports host-side argument/launch problems only (IRIS_OK == 0).  Problems
+ * that need the data to detect (bad slots, bad page ids, ...) are OR-ed into
+ * the caller's device `error_word` (int32, IRIS_ERR_* bits) by the kernels,
+ * which never read or write out of bounds: offending tokens / pages are
+ * skipped (write path) or replaced by page 0 (read path).
+ *
+ * Cache layout (identical to the reference, README.md:76-84):
+ *   k_data, v_data   [num_pages, page_size, Hkv, D/2]   uint8, low nibble first,
+ *                                                      signed INT4 in [-7, 7]
+ *   k_scale, v_scale [num_pages, page_size, Hkv, D/32]  fp16, one per 32 values
+ */
+#ifndef IRIS_B200_H_
+#define IRIS_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define IRIS_API __attribute__((visibility("default")))
+#else
+#define IRIS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes returned by the entry points ------------------------- */
+#define IRIS_OK 0
+#define IRIS_EINVAL 1          /* bad argument (shape / null pointer)            */
+#define IRIS_EUNSUPPORTED 2    /* shape outside the kernel's supported set        */
+#define IRIS_EALIGN 3          /* a pointer is not aligned as required            */
+#define IRIS_ECUDA 4           /* a CUDA runtime / driver call failed             */
+#define IRIS_EWORKSPACE 5      /* workspace too small                             */
+
+/* ---- bits OR-ed into the device error word ------------------------------ */
+#define IRIS_ERR_SLOT_RANGE 0x1        /* slot >= num_pages*page_size        (IndexError) */
+#define IRIS_ERR_POS_NEGATIVE 0x2      /* position < 0                       (IndexError) */
+#define IRIS_ERR_POS_RANGE 0x4         /* position >= max_position           (IndexError) */
+#define IRIS_ERR_DUP_SLOT 0x8          /* two tokens target one slot         (ValueError) */
+#define IRIS_ERR_SEQ_LEN 0x10          /* seq_len <= 0                       (ValueError) */
+#define IRIS_ERR_BLOCK_TABLE 0x20      /* block_table row shorter than needed (ValueError) */
+#define IRIS_ERR_PAGE_ID 0x40          /* page id outside [0, num_pages)     (IndexError) */
+#define IRIS_ERR_PIPELINE_TIMEOUT 0x80 /* a bounded wait gave up             (RuntimeError) */
+
+/* Library version (major*10000 + minor*100 + patch). */
+IRIS_API int iris_b200_version(void);
+
+/* Human-readable text for a status code. */
+IRIS_API const char* iris_b200_status_string(int status);
+
+/* Name and text of the last CUDA error an entry point of this library hit on
+ * the calling thread ("" if none); explains an IRIS_ECUDA status. */
+IRIS_API const char* iris_b200_last_cuda_error(void);
+
+/* ======================================================================
+ * WRITE PATH
+ * ====================================================================== */
+
+/* Bytes of device workspace iris_b200_append_check needs (slot bitmap). */
+IRIS_API size_t iris_b200_append_check_workspace_bytes(int64_t num_pages, int32_t page_size);
+
+/*
+ * Range / duplicate validation of an append batch, on the device.  Replaces
+ * the host-synchronising checks of fused_kv.py:741-759 (torch.unique +
+ * three any() calls).  For every token with slot >= 0 it checks
+ * slot < num_pages*page_size, 0 <= position < max_position, and that no two
+ * tokens share a slot, OR-ing IRIS_ERR_* bits into *error_word.  `workspace`
+ * (>= iris_b200_append_check_workspace_bytes) is cleared by this call.
+ */
+IRIS_API int iris_b200_append_check(const int32_t* positions, const int32_t* slot_mapping, int64_t num_tokens,
+                           int64_t max_position, int64_t num_pages, int32_t page_size, void* workspace,
+                           size_t workspace_bytes, int32_t* error_word, void* stream);
+
+/*
+ * Fused RoPE(K) + group-32 symmetric INT4 quantisation of K and V + low-
+ * nibble-first packing + paged append.  Replaces the _rope_int4_paged_append
+ * launch of fused_kv.py:766-780; bit-exact with torch_eager_append
+ * (torch_eager_kv.py:110-337): identical packed bytes and fp16 scales.
+ *
+ *   key, value  [num_tokens, num_kv_heads, head_dim] fp16
+ *   positions, slot_mapping [num_tokens] int32 (slot < 0: token skipped)
+ *   cos_cache, sin_cache [max_position, head_dim/2] fp16 (rotary_dim == head_dim)
+ *   head_dim % 64 == 0, group size 32.
+ * Slots / positions out of range are skipped and reported in *error_word
+ * (may be NULL).  Duplicate slots are not detected here (use
+ * iris_b200_append_check first).
+ */
+IRIS_API int iris_b200_rope_int4_paged_append(const void* key, const void* value, const int32_t* positions,
+                                     const int32_t* slot_mapping, const void* cos_cache, const void* sin_cache,
+                                     void* k_data, void* v_data, void* k_scale, void* v_scale, int64_t num_tokens,
+                                     int32_t num_kv_heads, int32_t head_dim, int64_t max_position,
+                                     int64_t num_pages, int32_t page_size, int32_t* error_word, void* stream);
+
+/* ======================================================================
+ * READ PATH
+ * ====================================================================== */
+
+/* Output forms of the decode. */
+#define IRIS_DECODE_OUT_FP16 0 /* output [B, Hq, D] fp16 = softmax(QK^T) V (reference form) */
+#define IRIS_DECODE_OUT_LSE 1  /* out_o [B, Hq, D] fp32 normalised + out_lse [B, Hq] fp32,
+                                  log2-sum-exp2 of the scaled logits (for split-context merge) */
+
+/* Bytes of device workspace iris_b200_int4_paged_decode needs. */
+IRIS_API size_t iris_b200_decode_workspace_bytes(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                        int32_t device);
+
+/*
+ * INT4 paged decode attention (one query token per sequence, GQA/MQA/MHA).
+ * Replaces the _int4_paged_decode_attention launch of
+ * fused_attention.py:508-524 with the semantics of
+ * torch_eager_int4_paged_decode_attention (torch_eager_attention.py:154-239):
+ * page lookup, nibble unpack, group dequantisation, QK, softmax and PV with
+ * FP32 accumulation.  Work is split over the GPU's SMs in page units
+ * (split-KV); partial (m, l, O) records live in `workspace` and are merged by
+ * a combine kernel in the same call.
+ *
+ *   query        [B, Hq, D] fp16                 D in {64, 128}
+ *   block_table  int32, row b at block_table + b*block_table_stride,
+ *                max_pages_per_seq valid columns
+ *   seq_lens     [B] int32 (> 0)
+ *   page_size 16, group 32, Hq % Hkv == 0, Hq/Hkv <= 16
+ *   softmax_scale > 0 (the reference's default is D^-0.5)
+ *   out_mode IRIS_DECODE_OUT_FP16: `output` [B, Hq, D] fp16, out_lse unused
+ *   out_mode IRIS_DECODE_OUT_LSE : `output` [B, Hq, D] fp32, out_lse [B, Hq] fp32
+ * k_data / v_data / k_scale / v_scale must be 16-byte aligned.
+ */
+IRIS_API int iris_b200_int4_paged_decode(const void* query, const void* k_data, const void* v_data, const void* k_scale,
+                                const void* v_scale, const int32_t* block_table, int64_t block_table_stride,
+                                const int32_t* seq_lens, void* output, float* out_lse, int32_t out_mode,
+                                int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                int64_t num_pages, int32_t page_size, int32_t max_pages_per_seq,
+                                float softmax_scale, void* workspace, size_t workspace_bytes, int32_t* error_word,
+                                void* stream);
+
+/*
+ * Merge `num_parts` log-sum-exp-form partial results (as produced with
+ * IRIS_DECODE_OUT_LSE) into the final fp16 output:
+ *   parts_o [num_parts, rows, D] fp32, parts_lse [num_parts, rows] fp32,
+ *   output [rows, D] fp16, rows = B*Hq.
+ * Used after an all-gather of per-GPU partials in split-context decode.  No
+ * counterpart in the reference (split-KV is out of its scope, README.md:425).
+ */
+IRIS_API int iris_b200_merge_lse_partials(const float* parts_o, const float* parts_lse, int32_t num_parts, int64_t rows,
+                                 int32_t head_dim, void* output, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IRIS_B200_H_ */

@@ -1,0 +1,362 @@
+// Fused RoPE(K) + group-32 symmetric INT4 quantisation + low-nibble-first
+// packing + paged append, for sm_100a.
+//
+// Replaces the reference kernel _rope_int4_paged_append
+// (src/iris_kernel/fused_kv.py:419-597) and reproduces, bit for bit, the
+// eager semantics of torch_eager_append (src/iris_kernel/torch_eager_kv.py:
+// 110-337): RoPE with an fp16 rounding after every op (:38-47), fp32 group
+// absmax, scale = fp16(max(amax / 7, 2^-14)) with an IEEE division (:69-81),
+// q = clamp(rint(x / scale), -7, 7) with an IEEE division and
+// round-half-to-even (:83-86), byte = q[2i] & 0xF | (q[2i+1] & 0xF) << 4
+// (:104-107).
+//
+// Layout of the work: one thread owns 8 consecutive dims (one 16-byte fp16
+// vector) of one (token, kv-head) row, for both K and V.  A row is D/8
+// threads; a 32-dim quantisation group is 4 adjacent lanes, reduced with two
+// xor-shuffles.  Loads are 128-bit and coalesced, packed stores are 32-bit
+// per thread (64 contiguous bytes per row for D=128) and the row's scales
+// leave in one vector store.  The kernel is HBM-bound: per (token, head) it
+// moves 4D bytes in and D + D/8 bytes out.
+#include "common.cuh"
+
+namespace iris {
+
+struct AppendParams {
+  const __half* key;
+  const __half* value;
+  const int32_t* positions;
+  const int32_t* slots;
+  const __half* cos_cache;
+  const __half* sin_cache;
+  uint8_t* k_data;
+  uint8_t* v_data;
+  __half* k_scale;
+  __half* v_scale;
+  int64_t num_tokens;
+  int64_t max_position;
+  int64_t num_slots;  // num_pages * page_size
+  int32_t num_heads;
+  int32_t page_size;
+  int32_t* err;
+};
+
+IRIS_DEV uint4 ldg_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+IRIS_DEV __half habs_max8(const __half2 (&v)[4]) {
+  // NaN-propagating, like torch's amax.
+  __half2 m = __hmax2_nan(__habs2(v[0]), __habs2(v[1]));
+  m = __hmax2_nan(m, __hmax2_nan(__habs2(v[2]), __habs2(v[3])));
+  return __hmax_nan(__low2half(m), __high2half(m));
+}
+
+// fp16 group scale from the group's absmax, exactly as the eager reference.
+IRIS_DEV __half group_scale(__half amax) {
+  float s = __fdiv_rn(__half2float(amax), 7.0f);
+  const float tiny = 6.103515625e-05f;  // 2^-14 = torch.finfo(float16).tiny
+  s = (s < tiny) ? tiny : s;            // NaN stays NaN (torch clamp_min)
+  return __float2half_rn(s);
+}
+
+IRIS_DEV uint32_t quant_pack8(const __half2 (&v)[4], float scale) {
+  uint32_t word = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(v[i]);
+    int q0 = __float2int_rn(__fdiv_rn(f.x, scale));
+    int q1 = __float2int_rn(__fdiv_rn(f.y, scale));
+    q0 = min(7, max(-7, q0));
+    q1 = min(7, max(-7, q1));
+    word |= (static_cast<uint32_t>(q0) & 0xFu) << (8 * i);
+    word |= (static_cast<uint32_t>(q1) & 0xFu) << (8 * i + 4);
+  }
+  return word;
+}
+
+IRIS_DEV __half shfl_half(__half v, int src, uint32_t mask) {
+  unsigned short u = __half_as_ushort(v);
+  u = static_cast<unsigned short>(__shfl_sync(mask, static_cast<unsigned>(u), src));
+  return __ushort_as_half(u);
+}
+
+IRIS_DEV __half shfl_xor_half(__half v, int x) {
+  unsigned short u = __half_as_ushort(v);
+  u = static_cast<unsigned short>(__shfl_xor_sync(0xffffffffu, static_cast<unsigned>(u), x));
+  return __ushort_as_half(u);
+}
+
+template <int D>
+struct AppendCfg {
+  static constexpr int kTpr = D / 8;                            // threads per (token, head) row
+  // rows per CTA: as many as fit in 256 threads while keeping whole warps
+  static constexpr int kRowQuant = 32 / (kTpr % 32 == 0 ? 32 : (kTpr % 16 == 0 ? 16 : 8));
+  static constexpr int kRows = (256 / kTpr) / kRowQuant * kRowQuant;
+  static constexpr int kThreads = kRows * kTpr;
+  static constexpr int kHalf = kTpr / 2;                        // RoPE partner distance in chunks
+  // partner via shuffle when a row sits inside one warp at a power-of-two width
+  static constexpr bool kShuffle = kTpr <= 32 && (32 % kTpr) == 0;
+  static constexpr int kGroups = D / 32;
+  static constexpr bool kVecScale = kShuffle && (kGroups == 2 || kGroups == 4 || kGroups == 8);
+};
+
+template <int D>
+__global__ void __launch_bounds__(AppendCfg<D>::kThreads) rope_int4_append_kernel(const AppendParams p) {
+  using C = AppendCfg<D>;
+  const int tid = threadIdx.x;
+  const int c = tid % C::kTpr;  // chunk of 8 dims within the row
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * C::kRows + tid / C::kTpr;
+  const int64_t nrows = p.num_tokens * p.num_heads;
+  const bool in_range = row < nrows;
+  const int64_t tok = in_range ? row / p.num_heads : 0;
+  const int h = in_range ? static_cast<int>(row % p.num_heads) : 0;
+
+  int32_t slot = in_range ? __ldg(p.slots + tok) : -1;
+  int32_t pos = 0;
+  bool active = slot >= 0;
+  if (active) {
+    pos = __ldg(p.positions + tok);
+    int32_t bits = 0;
+    if (static_cast<int64_t>(slot) >= p.num_slots) bits |= IRIS_ERR_SLOT_RANGE;
+    if (pos < 0) bits |= IRIS_ERR_POS_NEGATIVE;
+    else if (static_cast<int64_t>(pos) >= p.max_position) bits |= IRIS_ERR_POS_RANGE;
+    if (bits) {
+      if (h == 0 && c == 0) set_error(p.err, bits);
+      active = false;  // never touch memory outside the cache / RoPE tables
+    }
+  }
+
+  // ---- loads (inactive rows read nothing and compute on zeros) ----
+  const bool lo_half = c < C::kHalf;
+  const int pair = lo_half ? c : c - C::kHalf;  // chunk index into cos/sin
+  uint4 kr = make_uint4(0, 0, 0, 0), vr = kr, cr = kr, sr = kr, kp = kr;
+  const int64_t rowoff = (tok * p.num_heads + h) * static_cast<int64_t>(D);
+  if (active) {
+    kr = ldg_nc_v4(p.key + rowoff + 8 * c);
+    vr = ldg_nc_v4(p.value + rowoff + 8 * c);
+    cr = ldg_nc_v4(p.cos_cache + static_cast<int64_t>(pos) * (D / 2) + 8 * pair);
+    sr = ldg_nc_v4(p.sin_cache + static_cast<int64_t>(pos) * (D / 2) + 8 * pair);
+    if constexpr (!C::kShuffle) {
+      kp = ldg_nc_v4(p.key + rowoff + 8 * (lo_half ? c + C::kHalf : c - C::kHalf));
+    }
+  }
+  if constexpr (C::kShuffle) {
+    kp.x = __shfl_xor_sync(0xffffffffu, kr.x, C::kHalf);
+    kp.y = __shfl_xor_sync(0xffffffffu, kr.y, C::kHalf);
+    kp.z = __shfl_xor_sync(0xffffffffu, kr.z, C::kHalf);
+    kp.w = __shfl_xor_sync(0xffffffffu, kr.w, C::kHalf);
+  }
+
+  // ---- RoPE, fp16 rounding after each op ----
+  // low half:  y = x1*cos - x2*sin   (own = x1, partner = x2)
+  // high half: y = x2*cos + x1*sin   (own = x2, partner = x1)
+  // written as own*cos + (+-partner)*sin; negation is exact.
+  const __half2* kown = reinterpret_cast<const __half2*>(&kr);
+  const __half2* kpar = reinterpret_cast<const __half2*>(&kp);
+  const __half2* cs = reinterpret_cast<const __half2*>(&cr);
+  const __half2* sn = reinterpret_cast<const __half2*>(&sr);
+  __half2 kv[4], vv[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 par = lo_half ? __hneg2(kpar[i]) : kpar[i];
+    kv[i] = __hadd2(__hmul2_rn(kown[i], cs[i]), __hmul2_rn(par, sn[i]));
+    vv[i] = reinterpret_cast<const __half2*>(&vr)[i];
+  }
+
+  // ---- group absmax over 4 lanes, fp16 scales ----
+  __half kmax = habs_max8(kv), vmax = habs_max8(vv);
+  kmax = __hmax_nan(kmax, shfl_xor_half(kmax, 1));
+  vmax = __hmax_nan(vmax, shfl_xor_half(vmax, 1));
+  kmax = __hmax_nan(kmax, shfl_xor_half(kmax, 2));
+  vmax = __hmax_nan(vmax, shfl_xor_half(vmax, 2));
+  const __half ks = group_scale(kmax), vs = group_scale(vmax);
+
+  const uint32_t kword = quant_pack8(kv, __half2float(ks));
+  const uint32_t vword = quant_pack8(vv, __half2float(vs));
+
+  // ---- stores ----
+  const int64_t page = active ? slot / p.page_size : 0;
+  const int64_t off = active ? slot % p.page_size : 0;
+  const int64_t crow = (page * p.page_size + off) * p.num_heads + h;  // cache row
+  if (active) {
+    reinterpret_cast<uint32_t*>(p.k_data + crow * (D / 2))[c] = kword;
+    reinterpret_cast<uint32_t*>(p.v_data + crow * (D / 2))[c] = vword;
+  }
+  if constexpr (C::kVecScale) {
+    // gather the row's group scales into lane c == 0 and store them at once
+    const int lane = tid & 31;
+    const int base = lane - c;
+    __half kg[C::kGroups], vg[C::kGroups];
+#pragma unroll
+    for (int g = 0; g < C::kGroups; ++g) {
+      kg[g] = shfl_half(ks, base + 4 * g, 0xffffffffu);
+      vg[g] = shfl_half(vs, base + 4 * g, 0xffffffffu);
+    }
+    if (active && c == 0) {
+      __half* kdst = p.k_scale + crow * C::kGroups;
+      __half* vdst = p.v_scale + crow * C::kGroups;
+      if constexpr (C::kGroups == 2) {
+        *reinterpret_cast<__half2*>(kdst) = __halves2half2(kg[0], kg[1]);
+        *reinterpret_cast<__half2*>(vdst) = __halves2half2(vg[0], vg[1]);
+      } else if constexpr (C::kGroups == 4) {
+        uint2 kk, vvv;
+        kk.x = h2_as_u32(__halves2half2(kg[0], kg[1]));
+        kk.y = h2_as_u32(__halves2half2(kg[2], kg[3]));
+        vvv.x = h2_as_u32(__halves2half2(vg[0], vg[1]));
+        vvv.y = h2_as_u32(__halves2half2(vg[2], vg[3]));
+        *reinterpret_cast<uint2*>(kdst) = kk;
+        *reinterpret_cast<uint2*>(vdst) = vvv;
+      } else {
+        uint4 kk, vvv;
+        kk.x = h2_as_u32(__halves2half2(kg[0], kg[1]));
+        kk.y = h2_as_u32(__halves2half2(kg[2], kg[3]));
+        kk.z = h2_as_u32(__halves2half2(kg[4], kg[5]));
+        kk.w = h2_as_u32(__halves2half2(kg[6], kg[7]));
+        vvv.x = h2_as_u32(__halves2half2(vg[0], vg[1]));
+        vvv.y = h2_as_u32(__halves2half2(vg[2], vg[3]));
+        vvv.z = h2_as_u32(__halves2half2(vg[4], vg[5]));
+        vvv.w = h2_as_u32(__halves2half2(vg[6], vg[7]));
+        *reinterpret_cast<uint4*>(kdst) = kk;
+        *reinterpret_cast<uint4*>(vdst) = vvv;
+      }
+    }
+  } else {
+    if (active && (c & 3) == 0) {
+      p.k_scale[crow * C::kGroups + c / 4] = ks;
+      p.v_scale[crow * C::kGroups + c / 4] = vs;
+    }
+  }
+}
+
+// One thread per token: range checks and duplicate detection through a
+// slot bitmap (one bit per cache slot, cleared by the caller-side memset).
+__global__ void append_check_kernel(const int32_t* __restrict__ positions, const int32_t* __restrict__ slots,
+                                    int64_t num_tokens, int64_t max_position, int64_t num_slots,
+                                    uint32_t* __restrict__ bitmap, int32_t* err) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= num_tokens) return;
+  const int32_t s = slots[i];
+  if (s < 0) return;
+  int32_t bits = 0;
+  if (static_cast<int64_t>(s) >= num_slots) {
+    bits |= IRIS_ERR_SLOT_RANGE;
+  } else {
+    const uint32_t bit = 1u << (s & 31);
+    if (atomicOr(bitmap + (s >> 5), bit) & bit) bits |= IRIS_ERR_DUP_SLOT;
+  }
+  const int32_t pos = positions[i];
+  if (pos < 0) bits |= IRIS_ERR_POS_NEGATIVE;
+  else if (static_cast<int64_t>(pos) >= max_position) bits |= IRIS_ERR_POS_RANGE;
+  if (bits) set_error(err, bits);
+}
+
+template <int D>
+static cudaError_t launch_append(const AppendParams& p, cudaStream_t stream) {
+  using C = AppendCfg<D>;
+  const int64_t rows = p.num_tokens * p.num_heads;
+  const int64_t blocks = (rows + C::kRows - 1) / C::kRows;
+  if (blocks == 0) return cudaSuccess;
+  if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
+  rope_int4_append_kernel<D><<<static_cast<unsigned>(blocks), C::kThreads, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace iris
+
+using namespace iris;
+
+static bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+extern "C" size_t iris_b200_append_check_workspace_bytes(int64_t num_pages, int32_t page_size) {
+  if (num_pages < 0 || page_size <= 0) return 0;
+  const int64_t slots = num_pages * page_size;
+  return static_cast<size_t>(((slots + 31) / 32) * 4);
+}
+
+extern "C" int iris_b200_append_check(const int32_t* positions, const int32_t* slot_mapping, int64_t num_tokens,
+                                      int64_t max_position, int64_t num_pages, int32_t page_size, void* workspace,
+                                      size_t workspace_bytes, int32_t* error_word, void* stream) {
+  if (num_tokens < 0 || num_pages < 0 || page_size <= 0 || error_word == nullptr) return IRIS_EINVAL;
+  if (num_tokens == 0) return IRIS_OK;
+  if (positions == nullptr || slot_mapping == nullptr) return IRIS_EINVAL;
+  const size_t need = iris_b200_append_check_workspace_bytes(num_pages, page_size);
+  if (workspace_bytes < need || (need > 0 && workspace == nullptr)) return IRIS_EWORKSPACE;
+  if (!aligned(workspace, 4)) return IRIS_EALIGN;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  clear_stale_cuda_error();
+  if (need > 0) {
+    const cudaError_t e = cudaMemsetAsync(workspace, 0, need, s);
+    if (e != cudaSuccess) {
+      record_cuda_error(e, "cudaMemsetAsync(slot bitmap)");
+      return IRIS_ECUDA;
+    }
+  }
+  const int threads = 256;
+  const int64_t blocks = (num_tokens + threads - 1) / threads;
+  append_check_kernel<<<static_cast<unsigned>(blocks), threads, 0, s>>>(
+      positions, slot_mapping, num_tokens, max_position, num_pages * page_size, static_cast<uint32_t*>(workspace),
+      error_word);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    record_cuda_error(e, "append_check_kernel launch");
+    return IRIS_ECUDA;
+  }
+  return IRIS_OK;
+}
+
+extern "C" int iris_b200_rope_int4_paged_append(const void* key, const void* value, const int32_t* positions,
+                                                const int32_t* slot_mapping, const void* cos_cache,
+                                                const void* sin_cache, void* k_data, void* v_data, void* k_scale,
+                                                void* v_scale, int64_t num_tokens, int32_t num_kv_heads,
+                                                int32_t head_dim, int64_t max_position, int64_t num_pages,
+                                                int32_t page_size, int32_t* error_word, void* stream) {
+  if (num_tokens < 0 || num_kv_heads <= 0 || page_size <= 0 || num_pages < 0 || max_position < 0)
+    return IRIS_EINVAL;
+  if (head_dim <= 0 || head_dim % 64 != 0 || head_dim > 512) return IRIS_EUNSUPPORTED;
+  if (num_tokens == 0) return IRIS_OK;
+  const void* ptrs[] = {key, value, positions, slot_mapping, cos_cache, sin_cache, k_data, v_data, k_scale, v_scale};
+  for (const void* q : ptrs)
+    if (q == nullptr) return IRIS_EINVAL;
+  if (!aligned(key, 16) || !aligned(value, 16) || !aligned(cos_cache, 16) || !aligned(sin_cache, 16) ||
+      !aligned(k_data, 4) || !aligned(v_data, 4) || !aligned(k_scale, 16) || !aligned(v_scale, 16))
+    return IRIS_EALIGN;
+  AppendParams p;
+  p.key = static_cast<const __half*>(key);
+  p.value = static_cast<const __half*>(value);
+  p.positions = positions;
+  p.slots = slot_mapping;
+  p.cos_cache = static_cast<const __half*>(cos_cache);
+  p.sin_cache = static_cast<const __half*>(sin_cache);
+  p.k_data = static_cast<uint8_t*>(k_data);
+  p.v_data = static_cast<uint8_t*>(v_data);
+  p.k_scale = static_cast<__half*>(k_scale);
+  p.v_scale = static_cast<__half*>(v_scale);
+  p.num_tokens = num_tokens;
+  p.max_position = max_position;
+  p.num_slots = num_pages * page_size;
+  p.num_heads = num_kv_heads;
+  p.page_size = page_size;
+  p.err = error_word;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  clear_stale_cuda_error();
+  cudaError_t e;
+  switch (head_dim) {
+    case 64: e = launch_append<64>(p, s); break;
+    case 128: e = launch_append<128>(p, s); break;
+    case 192: e = launch_append<192>(p, s); break;
+    case 256: e = launch_append<256>(p, s); break;
+    case 320: e = launch_append<320>(p, s); break;
+    case 384: e = launch_append<384>(p, s); break;
+    case 448: e = launch_append<448>(p, s); break;
+    default: e = launch_append<512>(p, s); break;
+  }
+  if (e != cudaSuccess) {
+    record_cuda_error(e, "rope_int4_append_kernel launch");
+    return IRIS_ECUDA;
+  }
+  return IRIS_OK;
+}

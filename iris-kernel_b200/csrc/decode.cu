@@ -1,0 +1,960 @@
+// INT4 paged decode attention for sm_100a.
+//
+// Replaces the reference kernel _int4_paged_decode_attention
+// (src/iris_kernel/fused_attention.py:11-220); semantics are those of
+// torch_eager_int4_paged_decode_attention (src/iris_kernel/
+// torch_eager_attention.py:154-239): for every sequence b and query head h,
+// softmax(scale * q . k_l) weighted sum of v_l over the sequence's tokens,
+// with k/v dequantised from the paged INT4 cache and query head h reading KV
+// head h / (Hq/Hkv).
+//
+// Decomposition (split-KV, stream-K style).  The concatenation of all
+// sequences' pages is cut into R equal ranges of whole pages; CTA (r, hb)
+// walks range r for KV-head block hb.  A sequence that lies entirely inside
+// one range is finished by that CTA; pieces of a sequence that straddles
+// ranges leave (m, l, O) records that the combine kernel merges.  Work per
+// CTA is therefore equal whatever the length distribution.
+//
+// CTA = HB consumer warps (one per KV head of the block) + 1 producer warp.
+// The producer walks the page table and moves, per page and stage, each
+// head's 16 x D/2-byte K and V tiles with a 3-D TMA tensor copy (swizzled so
+// ldmatrix is conflict-free) and the page's K / V scale blocks with 1-D bulk
+// copies, into an S-deep ring of shared-memory stages guarded by mbarriers.
+//
+// Consumer math per page and head (16 tokens):
+//   S^T[tok][qh] = K[tok][:] . Q[qh][:]  as mma.m16n8k16 with M = tokens and
+//     N = query heads (8 per n-tile).  K stays in biased integer form
+//     (n + 1032 or 16 n + 1152 from a single LOP3 per half2) and each 32-dim
+//     group has its own accumulator, seeded with minus the bias correction, so
+//     the per-(token, group) scale is applied once in fp32 afterwards.
+//   online softmax in the log2 domain, P rounded to fp16 and transposed into
+//     the B operand with movmatrix; the V group scales multiply P (per token,
+//     per group) rather than the 4x larger V tile.
+//   O^T[dim][qh] += V^T[dim][tok] . P'^T[tok][qh] as mma.m16n8k16 with M =
+//     head dims, from ldmatrix.trans fragments converted to exact fp16 ints.
+// Head-dim permutations that make every 32-bit nibble word land on its MMA
+// fragment slots are undone when Q is loaded and when O is stored.
+#include <cstdio>
+#include <cstdlib>
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "common.cuh"
+
+namespace iris {
+
+static thread_local char g_last_error[256] = "";
+
+const char* record_cuda_error(cudaError_t e, const char* where) {
+  snprintf(g_last_error, sizeof(g_last_error), "%s: %s (%s)", where, cudaGetErrorName(e), cudaGetErrorString(e));
+  return g_last_error;
+}
+
+cudaError_t clear_stale_cuda_error() { return cudaGetLastError(); }
+
+constexpr int kPage = 16;
+#define kNegInf (-__int_as_float(0x7f800000))
+
+struct DecodeParams {
+  const __half* query;       // [B, Hq, D]
+  const uint8_t* k_scale;    // [NP, 16, Hkv, D/32] fp16, as bytes
+  const uint8_t* v_scale;
+  const int32_t* block_table;
+  int64_t bt_stride;
+  const int32_t* seq_lens;
+  void* out;                 // fp16 [B,Hq,D] or fp32 [B,Hq,D]
+  float* out_lse;            // [B,Hq] (LSE mode)
+  float* rec_o;              // [R, 2, Hq, D]
+  float* rec_lse;            // [R, 2, Hq]
+  const int32_t* prefix;     // [B+1] page prefix sums
+  const int32_t* range_seq;  // [R] first sequence of each range
+  const int32_t* meta;       // [0] total pages U, [1] ranges in use
+  int32_t* err;
+  int64_t num_pages;
+  int32_t batch, hq, hkv, max_pages;
+  int32_t hb;                // KV heads per CTA (= consumer warps)
+  int32_t qpk;               // query heads per KV head
+  int32_t stages;
+  int32_t out_mode;
+  float scale_log2;          // softmax_scale * log2(e)
+};
+
+template <int D>
+struct DecCfg {
+  static constexpr int kTileBytes = kPage * D / 2;  // one head's K (or V) tile of a page
+  static constexpr int kGroups = D / 32;
+  static constexpr int kScaleRowBytes = kGroups * 2;  // one (token, head) scale row
+};
+
+IRIS_DEV int64_t range_start(int64_t r, int64_t U, int64_t R) { return r * U / R; }
+IRIS_DEV int64_t range_of_page(int64_t u, int64_t U, int64_t R) { return ((u + 1) * R - 1) / U; }
+
+// ------------------------------------------------------------- plan kernel
+// Single CTA: page counts and prefix sums of the sequences, validation of
+// the lengths, and the first sequence of every range.
+__global__ void __launch_bounds__(1024) decode_plan_kernel(const int32_t* __restrict__ seq_lens, int32_t batch,
+                                                           int32_t max_pages, int32_t ranges, int32_t min_pages,
+                                                           int32_t* __restrict__ prefix,
+                                                           int32_t* __restrict__ range_seq,
+                                                           int32_t* __restrict__ meta, int32_t* err) {
+  __shared__ int32_t warp_tot[32];
+  __shared__ int32_t carry;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) carry = 0;
+  __syncthreads();
+  for (int base = 0; base < batch; base += 1024) {
+    const int b = base + tid;
+    int32_t np = 0;
+    if (b < batch) {
+      const int32_t L = seq_lens[b];
+      if (L <= 0) {
+        set_error(err, IRIS_ERR_SEQ_LEN);
+      } else {
+        np = (L + kPage - 1) / kPage;
+        if (np > max_pages) {
+          set_error(err, IRIS_ERR_BLOCK_TABLE);
+          np = max_pages;
+        }
+      }
+    }
+    int32_t x = np;  // inclusive warp scan
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_tot[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      int32_t w = warp_tot[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int32_t y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      warp_tot[lane] = w;  // inclusive over warps
+    }
+    __syncthreads();
+    const int32_t excl = carry + (warp ? warp_tot[warp - 1] : 0) + x - np;
+    if (b < batch) prefix[b] = excl;
+    __syncthreads();
+    if (tid == 0) carry += warp_tot[31];
+    __syncthreads();
+  }
+  const int32_t U = carry;
+  int32_t reff = 0;
+  if (U > 0) reff = min(ranges, max(1, (U + min_pages - 1) / min_pages));
+  if (tid == 0) {
+    prefix[batch] = U;
+    meta[0] = U;
+    meta[1] = reff;
+  }
+  __syncthreads();
+  for (int r = tid; r < reff; r += 1024) {
+    const int64_t u0 = range_start(r, U, reff);
+    int lo = 0, hi = batch;  // largest b with prefix[b] <= u0 (prefix[batch] = U > u0)
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (prefix[mid] <= u0) lo = mid;
+      else hi = mid;
+    }
+    range_seq[r] = lo;
+  }
+}
+
+// Per-warp attention state for one (sequence piece, KV head).
+template <int D, int NT>
+struct WarpState {
+  float o[NT][D / 16][4];
+  float m[NT][2];
+  float l[NT][2];
+  uint32_t qf[NT][D / 16][2];       // Q as mma B fragments (permuted dims, odd dims / 16)
+  float corr[NT][D / 32][2];        // bias correction per (group, column)
+};
+
+// Load query heads [h0, h0+qpk) of sequence b as B fragments and derive the
+// per-group bias corrections.  Lane (n = lane/4, t = lane%4) owns query head
+// n of each n-tile and dims 8t..8t+7 of every 32-dim group.
+template <int D, int NT>
+IRIS_DEV void load_query(WarpState<D, NT>& st, const __half* __restrict__ q_seq, int qpk, int lane) {
+  const int n = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int qh = nt * 8 + n;
+#pragma unroll
+    for (int g = 0; g < D / 32; ++g) {
+      uint4 raw = make_uint4(0, 0, 0, 0);
+      if (qh < qpk) raw = *reinterpret_cast<const uint4*>(q_seq + qh * D + g * 32 + t * 8);
+      const __half* e = reinterpret_cast<const __half*>(&raw);
+      const __half s16 = __float2half_rn(0.0625f);
+      __half eo[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) eo[i] = __hmul(e[2 * i + 1], s16);  // odd dims / 16 (exact)
+      st.qf[nt][2 * g + 0][0] = h2_as_u32(__halves2half2(e[0], e[4]));
+      st.qf[nt][2 * g + 0][1] = h2_as_u32(__halves2half2(eo[0], eo[2]));
+      st.qf[nt][2 * g + 1][0] = h2_as_u32(__halves2half2(e[2], e[6]));
+      st.qf[nt][2 * g + 1][1] = h2_as_u32(__halves2half2(eo[1], eo[3]));
+      float c = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        c += 1032.0f * __half2float(e[2 * i]);
+        c += 1152.0f * __half2float(eo[i]);
+      }
+      c += __shfl_xor_sync(0xffffffffu, c, 1);
+      c += __shfl_xor_sync(0xffffffffu, c, 2);
+      // column j of this lane's C fragment is query head 2t + j
+      st.corr[nt][g][0] = __shfl_sync(0xffffffffu, c, (2 * t) * 4);
+      st.corr[nt][g][1] = __shfl_sync(0xffffffffu, c, (2 * t + 1) * 4);
+    }
+#pragma unroll
+    for (int i = 0; i < D / 16; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) st.o[nt][i][j] = 0.f;
+    st.m[nt][0] = st.m[nt][1] = kNegInf;
+    st.l[nt][0] = st.l[nt][1] = 0.f;
+  }
+}
+
+// Lane offsets for the four 8x8 matrices of one ldmatrix.x4 over a swizzled
+// [16][D/2] tile: matrix (l>>3) covers token rows 8*((l>>3)&1).. and 16-byte
+// segment 2*i + (l>>4).
+template <int D>
+IRIS_DEV uint32_t tile_lane_offset(int lane, int i) {
+  const int mat = lane >> 3;
+  const int row = (lane & 7) + 8 * (mat & 1);
+  const int seg = 2 * i + (mat >> 1);
+  if constexpr (D == 128) {
+    return row * 64 + ((seg ^ ((row >> 1) & 3)) * 16);  // TMA SWIZZLE_64B
+  } else {
+    return row * 32 + ((seg ^ ((row >> 2) & 1)) * 16);  // TMA SWIZZLE_32B
+  }
+}
+
+// One page (16 tokens) of one KV head.
+template <int D, int NT>
+IRIS_DEV void process_page(WarpState<D, NT>& st, uint32_t ktile, uint32_t vtile, const __half* __restrict__ ksc,
+                           const __half* __restrict__ vsc, int scale_stride, int valid, float scale_log2, int lane) {
+  constexpr int G = D / 32;
+  const int g8 = lane >> 2, t = lane & 3;
+
+  // ---- K fragments: kw[grp][0] = token g8, kw[grp][1] = token g8 + 8 ----
+  uint32_t kw[G][2];
+#pragma unroll
+  for (int i = 0; i < G / 2; ++i) {
+    uint32_t r[4];
+    ldmatrix_x4(r, ktile + tile_lane_offset<D>(lane, i));
+    kw[2 * i][0] = r[0];
+    kw[2 * i][1] = r[1];
+    kw[2 * i + 1][0] = r[2];
+    kw[2 * i + 1][1] = r[3];
+  }
+
+  // K scales of this lane's two token rows
+  float ks[2][G];
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    const __half* sp = ksc + (g8 + 8 * rr) * scale_stride;
+    if constexpr (G == 4) {
+      const uint2 u = *reinterpret_cast<const uint2*>(sp);
+      const float2 a = __half22float2(u32_as_h2(u.x)), b = __half22float2(u32_as_h2(u.y));
+      ks[rr][0] = a.x; ks[rr][1] = a.y; ks[rr][2] = b.x; ks[rr][3] = b.y;
+    } else {
+      const float2 a = __half22float2(u32_as_h2(*reinterpret_cast<const uint32_t*>(sp)));
+      ks[rr][0] = a.x; ks[rr][1] = a.y;
+    }
+  }
+
+  const bool row0_ok = g8 < valid, row1_ok = (g8 + 8) < valid;
+
+  float p[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float acc[4] = {-st.corr[nt][g][0], -st.corr[nt][g][1], -st.corr[nt][g][0], -st.corr[nt][g][1]};
+#pragma unroll
+      for (int sub = 0; sub < 2; ++sub) {
+        const uint32_t w0 = kw[g][0] >> (8 * sub), w1 = kw[g][1] >> (8 * sub);
+        const uint32_t a[4] = {int4_lo_biased(w0), int4_lo_biased(w1), int4_hi_biased(w0), int4_hi_biased(w1)};
+        mma_16816(acc, a, st.qf[nt][2 * g + sub][0], st.qf[nt][2 * g + sub][1], acc);
+      }
+      s[0] = fmaf(ks[0][g], acc[0], s[0]);
+      s[1] = fmaf(ks[0][g], acc[1], s[1]);
+      s[2] = fmaf(ks[1][g], acc[2], s[2]);
+      s[3] = fmaf(ks[1][g], acc[3], s[3]);
+    }
+    // scaled logits, tail tokens masked
+    float x0 = row0_ok ? s[0] * scale_log2 : kNegInf;
+    float x1 = row0_ok ? s[1] * scale_log2 : kNegInf;
+    float x2 = row1_ok ? s[2] * scale_log2 : kNegInf;
+    float x3 = row1_ok ? s[3] * scale_log2 : kNegInf;
+    float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+    }
+    const float mn0 = fmaxf(st.m[nt][0], mx0), mn1 = fmaxf(st.m[nt][1], mx1);
+    const bool grow = (mn0 > st.m[nt][0]) || (mn1 > st.m[nt][1]);
+    if (__any_sync(0xffffffffu, grow)) {
+      const float c0 = ex2(st.m[nt][0] - mn0), c1 = ex2(st.m[nt][1] - mn1);  // ex2(-inf) = 0
+#pragma unroll
+      for (int i = 0; i < D / 16; ++i) {
+        st.o[nt][i][0] *= c0;
+        st.o[nt][i][1] *= c1;
+        st.o[nt][i][2] *= c0;
+        st.o[nt][i][3] *= c1;
+      }
+      st.l[nt][0] *= c0;
+      st.l[nt][1] *= c1;
+      st.m[nt][0] = mn0;
+      st.m[nt][1] = mn1;
+    }
+    p[nt][0] = ex2(x0 - st.m[nt][0]);
+    p[nt][1] = ex2(x1 - st.m[nt][1]);
+    p[nt][2] = ex2(x2 - st.m[nt][0]);
+    p[nt][3] = ex2(x3 - st.m[nt][1]);
+    st.l[nt][0] += p[nt][0] + p[nt][2];
+    st.l[nt][1] += p[nt][1] + p[nt][3];
+  }
+
+  // ---- V scales for tokens 2t, 2t+1, 2t+8, 2t+9, zeroed past the tail ----
+  uint32_t sv01[G], sv89[G];  // half2 (token a, token b) per group
+  {
+    uint32_t raw[4][G / 2];
+    const int toks[4] = {2 * t, 2 * t + 1, 2 * t + 8, 2 * t + 9};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const __half* sp = vsc + toks[k] * scale_stride;
+      const bool ok = toks[k] < valid;
+      if constexpr (G == 4) {
+        uint2 u = *reinterpret_cast<const uint2*>(sp);
+        raw[k][0] = ok ? u.x : 0u;
+        raw[k][1] = ok ? u.y : 0u;
+      } else {
+        const uint32_t u = *reinterpret_cast<const uint32_t*>(sp);
+        raw[k][0] = ok ? u : 0u;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < G / 2; ++j) {
+      sv01[2 * j] = prmt(raw[0][j], raw[1][j], 0x5410);
+      sv01[2 * j + 1] = prmt(raw[0][j], raw[1][j], 0x7632);
+      sv89[2 * j] = prmt(raw[2][j], raw[3][j], 0x5410);
+      sv89[2 * j + 1] = prmt(raw[2][j], raw[3][j], 0x7632);
+    }
+  }
+
+  // ---- P^T as B operands (one per group: P scaled by that group's V scale) ----
+  uint32_t pb[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    pb[nt][0] = movmatrix_trans(h2_as_u32(__floats2half2_rn(p[nt][0], p[nt][1])));
+    pb[nt][1] = movmatrix_trans(h2_as_u32(__floats2half2_rn(p[nt][2], p[nt][3])));
+  }
+
+  // ---- V fragments and PV ----
+#pragma unroll
+  for (int i = 0; i < G / 2; ++i) {
+    uint32_t r[4];
+    ldmatrix_x4_trans(r, vtile + tile_lane_offset<D>(lane, i));
+    // r[0] = (tokens 2t,2t+1; group 2i), r[1] = (tokens 2t+8,2t+9; group 2i),
+    // r[2], r[3] likewise for group 2i+1
+#pragma unroll
+    for (int gg = 0; gg < 2; ++gg) {
+      const int g = 2 * i + gg;
+      const uint32_t wa = r[2 * gg], wb = r[2 * gg + 1];
+      uint32_t bv[NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        bv[nt][0] = h2_as_u32(__hmul2(u32_as_h2(pb[nt][0]), u32_as_h2(sv01[g])));
+        bv[nt][1] = h2_as_u32(__hmul2(u32_as_h2(pb[nt][1]), u32_as_h2(sv89[g])));
+      }
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const uint32_t xa = wa >> (8 * jj), xb = wb >> (8 * jj);
+        const uint32_t a[4] = {int4_lo_exact(xa), int4_hi_exact(xa), int4_lo_exact(xb), int4_hi_exact(xb)};
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma_16816(st.o[nt][2 * g + jj], a, bv[nt][0], bv[nt][1], st.o[nt][2 * g + jj]);
+      }
+    }
+  }
+}
+
+// Finish a (sequence piece, KV head): reduce l over the lane's token rows,
+// then either write the final output or a partial record.
+template <int D, int NT>
+IRIS_DEV void finish_piece(const DecodeParams& p, WarpState<D, NT>& st, int b, int kvh, bool complete, int64_t rec,
+                           int lane) {
+  const int g8 = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    float l0 = st.l[nt][0], l1 = st.l[nt][1];
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+    }
+    const float inv[2] = {1.0f / l0, 1.0f / l1};
+    const float lse[2] = {st.m[nt][0] + lg2(l0), st.m[nt][1] + lg2(l1)};
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int qh_local = nt * 8 + 2 * t + j;
+      if (qh_local >= p.qpk) continue;
+      const int qh = kvh * p.qpk + qh_local;
+#pragma unroll
+      for (int g = 0; g < D / 32; ++g) {
+        // dims 32g + 4*g8 + {0,1,2,3} from m-tiles (2g, 2g+1), rows (g8, g8+8)
+        const float v0 = st.o[nt][2 * g][j] * inv[j];
+        const float v1 = st.o[nt][2 * g][2 + j] * inv[j];
+        const float v2 = st.o[nt][2 * g + 1][j] * inv[j];
+        const float v3 = st.o[nt][2 * g + 1][2 + j] * inv[j];
+        const int d = 32 * g + 4 * g8;
+        if (complete && p.out_mode == IRIS_DECODE_OUT_FP16) {
+          __half* dst = static_cast<__half*>(p.out) + (static_cast<int64_t>(b) * p.hq + qh) * D + d;
+          uint2 u;
+          u.x = h2_as_u32(__floats2half2_rn(v0, v1));
+          u.y = h2_as_u32(__floats2half2_rn(v2, v3));
+          *reinterpret_cast<uint2*>(dst) = u;
+        } else {
+          float* dst = complete ? static_cast<float*>(p.out) + (static_cast<int64_t>(b) * p.hq + qh) * D + d
+                                : p.rec_o + (rec * p.hq + qh) * D + d;
+          *reinterpret_cast<float4*>(dst) = make_float4(v0, v1, v2, v3);
+        }
+      }
+      if (g8 == 0) {
+        if (complete) {
+          if (p.out_mode == IRIS_DECODE_OUT_LSE) p.out_lse[static_cast<int64_t>(b) * p.hq + qh] = lse[j];
+        } else {
+          p.rec_lse[rec * p.hq + qh] = lse[j];
+        }
+      }
+    }
+  }
+}
+
+template <int D, int NT>
+__global__ void __launch_bounds__(9 * 32) decode_kernel(const __grid_constant__ CUtensorMap kmap,
+                                                        const __grid_constant__ CUtensorMap vmap,
+                                                        const DecodeParams p) {
+  using C = DecCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  const int hblk = blockIdx.x;
+  const int r = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int HB = p.hb;
+  const int S = p.stages;
+  const int U = p.meta[0], R = p.meta[1];
+  if (r >= R) return;  // uniform per CTA
+
+  const int scale_block = kPage * p.hkv * C::kGroups * 2;  // bytes of one page's K (or V) scales
+  const int stage_bytes = ((2 * HB * C::kTileBytes + 2 * scale_block) + 1023) & ~1023;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * stage_bytes);
+  uint64_t* empty = full + S;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, HB);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  const int64_t u0 = range_start(r, U, R), u1 = range_start(r + 1, U, R);
+  const int b_first = p.range_seq[r];
+
+  if (warp == HB) {
+    // ======================= producer warp =======================
+    if (lane == 0) {
+      prefetch_tensormap(&kmap);
+      prefetch_tensormap(&vmap);
+      const uint32_t tx = 2 * HB * C::kTileBytes + 2 * scale_block;
+      uint32_t it = 0;
+      bool alive = true;
+      int b = b_first;
+      int64_t u = u0;
+      while (alive && u < u1) {
+        const int64_t ps = p.prefix[b], pe = p.prefix[b + 1];
+        if (pe <= u) { ++b; continue; }
+        const int64_t hi = pe < u1 ? pe : u1;
+        const int32_t* bt_row = p.block_table + static_cast<int64_t>(b) * p.bt_stride;
+        for (int64_t pg = u; pg < hi; ++pg, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          if (!mbar_wait_bounded(empty + s, ph ^ 1, p.err)) { alive = false; break; }
+          int32_t pid = bt_row[pg - ps];
+          if (pid < 0 || static_cast<int64_t>(pid) >= p.num_pages) {
+            set_error(p.err, IRIS_ERR_PAGE_ID);
+            pid = 0;
+          }
+          uint8_t* st = smem + s * stage_bytes;
+          mbar_arrive_expect_tx(full + s, tx);
+          for (int h = 0; h < HB; ++h) {
+            const int kvh = hblk * HB + h;
+            tma_load_3d(st + h * C::kTileBytes, &kmap, 0, kvh, pid * kPage, full + s);
+            tma_load_3d(st + (HB + h) * C::kTileBytes, &vmap, 0, kvh, pid * kPage, full + s);
+          }
+          uint8_t* sc = st + 2 * HB * C::kTileBytes;
+          bulk_g2s(sc, p.k_scale + static_cast<int64_t>(pid) * scale_block, scale_block, full + s);
+          bulk_g2s(sc + scale_block, p.v_scale + static_cast<int64_t>(pid) * scale_block, scale_block, full + s);
+        }
+        u = hi;
+        ++b;
+      }
+      // drain: every copy this CTA issued has landed before it exits
+      const uint32_t last = it;
+      const uint32_t first = last > static_cast<uint32_t>(S) ? last - S : 0;
+      for (uint32_t k = first; k < last; ++k) mbar_wait_bounded(full + (k % S), (k / S) & 1, p.err);
+    }
+    return;
+  }
+
+  // ========================= consumer warps =========================
+  const int kvh = hblk * HB + warp;
+  WarpState<D, NT> st;
+  const uint32_t smem_base = smem_u32(smem);
+  uint32_t it = 0;
+  int b = b_first;
+  int64_t u = u0;
+  while (u < u1) {
+    const int64_t ps = p.prefix[b], pe = p.prefix[b + 1];
+    if (pe <= u) { ++b; continue; }
+    const int64_t hi = pe < u1 ? pe : u1;
+    const int L = min(p.seq_lens[b], p.max_pages * kPage);
+    load_query<D, NT>(st, p.query + (static_cast<int64_t>(b) * p.hq + kvh * p.qpk) * D, p.qpk, lane);
+    bool alive = true;
+    for (int64_t pg = u; pg < hi; ++pg, ++it) {
+      const int s = it % S;
+      const uint32_t ph = (it / S) & 1;
+      if (!mbar_wait_bounded(full + s, ph, p.err)) { alive = false; break; }
+      const uint32_t stb = smem_base + s * stage_bytes;
+      const uint8_t* sc = smem + s * stage_bytes + 2 * HB * C::kTileBytes;
+      const int valid = L - static_cast<int>(pg - ps) * kPage;
+      process_page<D, NT>(st, stb + warp * C::kTileBytes, stb + (HB + warp) * C::kTileBytes,
+                          reinterpret_cast<const __half*>(sc) + kvh * C::kGroups,
+                          reinterpret_cast<const __half*>(sc + scale_block) + kvh * C::kGroups,
+                          p.hkv * C::kGroups, valid < kPage ? valid : kPage, p.scale_log2, lane);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty + s);
+    }
+    if (!alive) return;
+    const bool complete = (ps >= u0) && (pe <= u1);
+    const int64_t rec = static_cast<int64_t>(r) * 2 + (u == u0 ? 0 : 1);
+    finish_piece<D, NT>(p, st, b, kvh, complete, rec, lane);
+    u = hi;
+    ++b;
+  }
+}
+
+// ---------------------------------------------------------- combine kernel
+// One CTA of D/4 threads per (sequence, query head): merges the records of
+// every range the sequence touches.  Sequences finished inside one range
+// were written by the decode kernel and are skipped.
+template <int D>
+__global__ void __launch_bounds__(D / 4) decode_combine_kernel(const DecodeParams p) {
+  const int b = blockIdx.x, qh = blockIdx.y, t = threadIdx.x;
+  const int64_t U = p.meta[0], R = p.meta[1];
+  const int64_t ps = p.prefix[b], pe = p.prefix[b + 1];
+  if (pe <= ps) return;
+  const int64_t f = range_of_page(ps, U, R), l = range_of_page(pe - 1, U, R);
+  if (f == l) return;
+  float mx = kNegInf;
+  for (int64_t r = f; r <= l; ++r) {
+    const int64_t rec = r * 2 + ((r == f && ps > range_start(r, U, R)) ? 1 : 0);
+    mx = fmaxf(mx, p.rec_lse[rec * p.hq + qh]);
+  }
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float wsum = 0.f;
+  for (int64_t r = f; r <= l; ++r) {
+    const int64_t rec = r * 2 + ((r == f && ps > range_start(r, U, R)) ? 1 : 0);
+    const float w = ex2(p.rec_lse[rec * p.hq + qh] - mx);
+    const float4 o = *reinterpret_cast<const float4*>(p.rec_o + (rec * p.hq + qh) * D + 4 * t);
+    acc.x = fmaf(w, o.x, acc.x);
+    acc.y = fmaf(w, o.y, acc.y);
+    acc.z = fmaf(w, o.z, acc.z);
+    acc.w = fmaf(w, o.w, acc.w);
+    wsum += w;
+  }
+  const float inv = 1.0f / wsum;
+  const int64_t orow = static_cast<int64_t>(b) * p.hq + qh;
+  if (p.out_mode == IRIS_DECODE_OUT_FP16) {
+    uint2 u;
+    u.x = h2_as_u32(__floats2half2_rn(acc.x * inv, acc.y * inv));
+    u.y = h2_as_u32(__floats2half2_rn(acc.z * inv, acc.w * inv));
+    *reinterpret_cast<uint2*>(static_cast<__half*>(p.out) + orow * D + 4 * t) = u;
+  } else {
+    *reinterpret_cast<float4*>(static_cast<float*>(p.out) + orow * D + 4 * t) =
+        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    if (t == 0) p.out_lse[orow] = mx + lg2(wsum);
+  }
+}
+
+// Merge of log-sum-exp partials from several producers (e.g. GPUs).
+__global__ void merge_lse_kernel(const float* __restrict__ parts_o, const float* __restrict__ parts_lse,
+                                 int32_t num_parts, int64_t rows, int32_t head_dim, __half* __restrict__ out) {
+  const int64_t row = blockIdx.x;
+  if (row >= rows) return;
+  float mx = kNegInf;
+  for (int k = 0; k < num_parts; ++k) mx = fmaxf(mx, parts_lse[k * rows + row]);
+  for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
+    float acc = 0.f, ws = 0.f;
+    for (int k = 0; k < num_parts; ++k) {
+      const float w = ex2(parts_lse[k * rows + row] - mx);
+      acc = fmaf(w, parts_o[(k * rows + row) * head_dim + d], acc);
+      ws += w;
+    }
+    out[row * head_dim + d] = __float2half_rn(acc / ws);
+  }
+}
+
+}  // namespace iris
+
+using namespace iris;
+
+// ------------------------------------------------------------- host side
+
+namespace {
+
+constexpr int kMinPagesPerRange = 4;
+constexpr int kSmemBudgetPerSm = 200 * 1024;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// 3-D view of k_data / v_data: (D/2 bytes, Hkv heads, NP*16 token rows); a
+// box is one head's 16 rows of one page.
+bool make_kv_map(CUtensorMap* map, const void* base, int D, int hkv, int64_t num_pages) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) return false;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(D / 2), static_cast<cuuint64_t>(hkv),
+                              static_cast<cuuint64_t>(num_pages) * kPage};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(D / 2), static_cast<cuuint64_t>(hkv) * (D / 2)};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(D / 2), 1u, static_cast<cuuint32_t>(kPage)};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUtensorMapSwizzle sw = (D == 128) ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// KV heads per CTA: the largest power of two <= max_hb dividing Hkv.
+// IRIS_DECODE_MAX_HB (1, 2, 4 or 8) overrides the default of 4 for tuning.
+int max_hb() {
+  static int v = [] {
+    const char* e = getenv("IRIS_DECODE_MAX_HB");
+    int x = e ? atoi(e) : 4;
+    return (x == 1 || x == 2 || x == 4 || x == 8) ? x : 4;
+  }();
+  return v;
+}
+
+int pick_hb(int hkv) {
+  for (int hb = max_hb(); hb >= 1; hb >>= 1)
+    if (hkv % hb == 0) return hb;
+  return 1;
+}
+
+struct LaunchShape {
+  int hb, nhb, stages, stage_bytes, smem, ranges, max_ranges;
+};
+
+int stage_bytes_for(int D, int hkv, int hb) {
+  const int tile = kPage * D / 2;
+  const int scale_block = kPage * hkv * (D / 32) * 2;
+  return ((2 * hb * tile + 2 * scale_block) + 1023) & ~1023;
+}
+
+int smem_for(int stages, int stage_bytes) { return stages * stage_bytes + 2 * stages * 8 + 1024; }
+
+int device_sms(int device) {
+  static std::mutex mu;
+  static std::map<int, int> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(device);
+  if (it != cache.end()) return it->second;
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || sms <= 0) {
+    cudaGetLastError();
+    return 148;  // not cached: no device visible (host-only use)
+  }
+  cache[device] = sms;
+  return sms;
+}
+
+// Upper bound on the number of ranges (sizes the workspace): at most
+// 16 consumer warps' worth of CTAs per SM.
+int max_ranges_for(int hkv, int sms) {
+  const int hb = pick_hb(hkv);
+  const int nhb = hkv / hb;
+  const int ctas = 16 / hb < 1 ? 1 : 16 / hb;
+  const int r = sms * ctas / nhb;
+  return r < 1 ? 1 : r;
+}
+
+// The dynamic shared memory limit is a per-kernel attribute shared by every
+// shape, so it only ever grows (a smaller shape must not lower it under a
+// larger cached one).
+template <int D, int NT>
+cudaError_t ensure_smem_attr(int device, int smem) {
+  static std::mutex mu;
+  static std::map<int, int> set_to;
+  std::lock_guard<std::mutex> lock(mu);
+  int& cur = set_to[device];
+  if (smem <= cur) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(decode_kernel<D, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess) cur = smem;
+  return e;
+}
+
+// Computed once per (D, NT, Hkv, device): later calls make no attribute or
+// occupancy queries, so the entry point can be captured in a CUDA graph
+// after its first (uncaptured) call.
+template <int D, int NT>
+LaunchShape compute_launch_shape(int hkv, int device) {
+  LaunchShape s;
+  const int sms = device_sms(device);
+  s.hb = pick_hb(hkv);
+  s.nhb = hkv / s.hb;
+  s.stage_bytes = stage_bytes_for(D, hkv, s.hb);
+  s.max_ranges = max_ranges_for(hkv, sms);
+  const int threads = (s.hb + 1) * 32;
+  int target = 16 / s.hb < 1 ? 1 : 16 / s.hb;
+  for (; target >= 1; --target) {
+    int stages = (kSmemBudgetPerSm / target - 1024 - 256) / s.stage_bytes;
+    stages = stages < 2 ? 2 : (stages > 10 ? 10 : stages);
+    const int smem = smem_for(stages, s.stage_bytes);
+    int occ = 0;
+    if (ensure_smem_attr<D, NT>(device, smem) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel<D, NT>, threads, smem) != cudaSuccess) {
+      cudaGetLastError();
+      occ = 0;
+    }
+    if (occ >= target || target == 1) {
+      s.stages = stages;
+      s.smem = smem;
+      int ranges = sms * (occ < target ? (occ > 0 ? occ : 1) : target) / s.nhb;
+      ranges = ranges < 1 ? 1 : ranges;
+      s.ranges = ranges > s.max_ranges ? s.max_ranges : ranges;
+      break;
+    }
+  }
+  return s;
+}
+
+template <int D, int NT>
+LaunchShape launch_shape(int hkv, int device) {
+  static std::mutex mu;
+  static std::map<std::pair<int, int>, LaunchShape> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(hkv, device);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  const LaunchShape s = compute_launch_shape<D, NT>(hkv, device);
+  cache[key] = s;
+  return s;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct Workspace {
+  int32_t* prefix;
+  int32_t* range_seq;
+  int32_t* meta;
+  float* rec_lse;
+  float* rec_o;
+  size_t bytes;
+};
+
+Workspace carve(void* base, int batch, int hq, int D, int ranges) {
+  Workspace w;
+  uint8_t* p = static_cast<uint8_t*>(base);
+  size_t off = 0;
+  w.prefix = reinterpret_cast<int32_t*>(p + off);
+  off += align256(sizeof(int32_t) * (batch + 1));
+  w.range_seq = reinterpret_cast<int32_t*>(p + off);
+  off += align256(sizeof(int32_t) * ranges);
+  w.meta = reinterpret_cast<int32_t*>(p + off);
+  off += 256;
+  w.rec_lse = reinterpret_cast<float*>(p + off);
+  off += align256(sizeof(float) * 2 * static_cast<size_t>(ranges) * hq);
+  w.rec_o = reinterpret_cast<float*>(p + off);
+  off += align256(sizeof(float) * 2 * static_cast<size_t>(ranges) * hq * D);
+  w.bytes = off;
+  return w;
+}
+
+template <int D, int NT>
+cudaError_t launch_decode(const CUtensorMap& km, const CUtensorMap& vm, DecodeParams p, int device,
+                          cudaStream_t stream, int32_t ranges_cap) {
+  const LaunchShape ls = launch_shape<D, NT>(p.hkv, device);
+  p.hb = ls.hb;
+  p.stages = ls.stages;
+  const int32_t ranges = ls.ranges < ranges_cap ? ls.ranges : ranges_cap;
+  cudaError_t e;
+  decode_plan_kernel<<<1, 1024, 0, stream>>>(p.seq_lens, p.batch, p.max_pages, ranges, kMinPagesPerRange,
+                                             const_cast<int32_t*>(p.prefix), const_cast<int32_t*>(p.range_seq),
+                                             const_cast<int32_t*>(p.meta), p.err);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    record_cuda_error(e, "decode_plan_kernel launch");
+    return e;
+  }
+  auto kern = decode_kernel<D, NT>;
+  e = ensure_smem_attr<D, NT>(device, ls.smem);  // no-op once raised
+  if (e != cudaSuccess) {
+    record_cuda_error(e, "cudaFuncSetAttribute(max dynamic smem)");
+    return e;
+  }
+  // head blocks of one range are adjacent in launch order: they share the
+  // page's scale sectors and DRAM rows
+  dim3 grid(ls.nhb, ranges);
+  kern<<<grid, (ls.hb + 1) * 32, ls.smem, stream>>>(km, vm, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    record_cuda_error(e, "decode_kernel launch");
+    return e;
+  }
+  dim3 cgrid(p.batch, p.hq);
+  decode_combine_kernel<D><<<cgrid, D / 4, 0, stream>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) record_cuda_error(e, "decode_combine_kernel launch");
+  return e;
+}
+
+}  // namespace
+
+extern "C" size_t iris_b200_decode_workspace_bytes(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                                                   int32_t head_dim, int32_t device) {
+  if (batch <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || (head_dim != 64 && head_dim != 128)) return 0;
+  return carve(nullptr, batch, num_q_heads, head_dim, max_ranges_for(num_kv_heads, device_sms(device))).bytes;
+}
+
+extern "C" int iris_b200_int4_paged_decode(const void* query, const void* k_data, const void* v_data,
+                                           const void* k_scale, const void* v_scale, const int32_t* block_table,
+                                           int64_t block_table_stride, const int32_t* seq_lens, void* output,
+                                           float* out_lse, int32_t out_mode, int32_t batch, int32_t num_q_heads,
+                                           int32_t num_kv_heads, int32_t head_dim, int64_t num_pages,
+                                           int32_t page_size, int32_t max_pages_per_seq, float softmax_scale,
+                                           void* workspace, size_t workspace_bytes, int32_t* error_word,
+                                           void* stream) {
+  if (batch < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || num_pages <= 0 || max_pages_per_seq < 0)
+    return IRIS_EINVAL;
+  if (page_size != kPage || (head_dim != 64 && head_dim != 128)) return IRIS_EUNSUPPORTED;
+  if (num_q_heads % num_kv_heads != 0) return IRIS_EINVAL;
+  const int qpk = num_q_heads / num_kv_heads;
+  if (qpk > 16) return IRIS_EUNSUPPORTED;
+  if (out_mode != IRIS_DECODE_OUT_FP16 && out_mode != IRIS_DECODE_OUT_LSE) return IRIS_EINVAL;
+  if (batch == 0) return IRIS_OK;
+  if (max_pages_per_seq > 0 && block_table_stride < max_pages_per_seq) return IRIS_EINVAL;
+  const void* ptrs[] = {query, k_data, v_data, k_scale, v_scale, seq_lens, output, workspace, error_word};
+  for (const void* q : ptrs)
+    if (q == nullptr) return IRIS_EINVAL;
+  if (max_pages_per_seq > 0 && block_table == nullptr) return IRIS_EINVAL;
+  if (out_mode == IRIS_DECODE_OUT_LSE && out_lse == nullptr) return IRIS_EINVAL;
+  if (!(softmax_scale > 0.0f) && !(softmax_scale < 0.0f)) return IRIS_EINVAL;
+  auto al = [](const void* q, uintptr_t a) { return reinterpret_cast<uintptr_t>(q) % a == 0; };
+  if (!al(k_data, 16) || !al(v_data, 16) || !al(k_scale, 16) || !al(v_scale, 16) || !al(query, 16) ||
+      !al(output, 16) || !al(workspace, 256))
+    return IRIS_EALIGN;
+
+  clear_stale_cuda_error();
+  int device = 0;
+  if (cudaError_t e0 = cudaGetDevice(&device); e0 != cudaSuccess) {
+    record_cuda_error(e0, "cudaGetDevice");
+    return IRIS_ECUDA;
+  }
+  const int32_t max_ranges = max_ranges_for(num_kv_heads, device_sms(device));
+  const Workspace ws = carve(workspace, batch, num_q_heads, head_dim, max_ranges);
+  if (workspace_bytes < ws.bytes) return IRIS_EWORKSPACE;
+
+  CUtensorMap km, vm;
+  if (!make_kv_map(&km, k_data, head_dim, num_kv_heads, num_pages) ||
+      !make_kv_map(&vm, v_data, head_dim, num_kv_heads, num_pages)) {
+    snprintf(iris::g_last_error, sizeof(iris::g_last_error), "cuTensorMapEncodeTiled failed (D=%d Hkv=%d pages=%lld)", head_dim,
+             num_kv_heads, static_cast<long long>(num_pages));
+    return IRIS_ECUDA;
+  }
+
+  DecodeParams p;
+  p.query = static_cast<const __half*>(query);
+  p.k_scale = static_cast<const uint8_t*>(k_scale);
+  p.v_scale = static_cast<const uint8_t*>(v_scale);
+  p.block_table = block_table;
+  p.bt_stride = block_table_stride;
+  p.seq_lens = seq_lens;
+  p.out = output;
+  p.out_lse = out_lse;
+  p.rec_o = ws.rec_o;
+  p.rec_lse = ws.rec_lse;
+  p.prefix = ws.prefix;
+  p.range_seq = ws.range_seq;
+  p.meta = ws.meta;
+  p.err = error_word;
+  p.num_pages = num_pages;
+  p.batch = batch;
+  p.hq = num_q_heads;
+  p.hkv = num_kv_heads;
+  p.max_pages = max_pages_per_seq;
+  p.hb = 0;
+  p.qpk = qpk;
+  p.stages = 0;
+  p.out_mode = out_mode;
+  p.scale_log2 = static_cast<float>(static_cast<double>(softmax_scale) * 1.4426950408889634);
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (head_dim == 128) {
+    e = qpk <= 8 ? launch_decode<128, 1>(km, vm, p, device, s, max_ranges)
+                 : launch_decode<128, 2>(km, vm, p, device, s, max_ranges);
+  } else {
+    e = qpk <= 8 ? launch_decode<64, 1>(km, vm, p, device, s, max_ranges)
+                 : launch_decode<64, 2>(km, vm, p, device, s, max_ranges);
+  }
+  return e == cudaSuccess ? IRIS_OK : IRIS_ECUDA;
+}
+
+extern "C" int iris_b200_merge_lse_partials(const float* parts_o, const float* parts_lse, int32_t num_parts,
+                                            int64_t rows, int32_t head_dim, void* output, void* stream) {
+  if (num_parts <= 0 || rows < 0 || head_dim <= 0 || parts_o == nullptr || parts_lse == nullptr || output == nullptr)
+    return IRIS_EINVAL;
+  if (rows == 0) return IRIS_OK;
+  clear_stale_cuda_error();
+  merge_lse_kernel<<<static_cast<unsigned>(rows), 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      parts_o, parts_lse, num_parts, rows, head_dim, static_cast<__half*>(output));
+  return cudaGetLastError() == cudaSuccess ? IRIS_OK : IRIS_ECUDA;
+}
+
+extern "C" const char* iris_b200_last_cuda_error(void) { return iris::g_last_error; }
+
+extern "C" int iris_b200_version(void) { return 100; }
+
+extern "C" const char* iris_b200_status_string(int status) {
+  switch (status) {
+    case IRIS_OK: return "ok";
+    case IRIS_EINVAL: return "invalid argument";
+    case IRIS_EUNSUPPORTED: return "unsupported shape";
+    case IRIS_EALIGN: return "pointer not aligned as required";
+    case IRIS_ECUDA: return "CUDA runtime error";
+    case IRIS_EWORKSPACE: return "workspace too small";
+    default: return "unknown status";
+  }
+}

@@ -1,0 +1,97 @@
+"""Per-device state shared by the wrappers: the device error word and the
+validation mode.
+
+The reference validates on the host with device->host synchronisations
+(``torch.unique`` / ``any()`` in fused_kv.py:741-759, one ``.item()`` per
+sequence in fused_attention.py:415-429).  Here the kernels check the data on
+the device and OR ``IRIS_ERR_*`` bits into an int32 error word:
+
+* ``"sync"`` (default): after launching, the wrapper reads the word once and
+  raises the reference's exception type.  The append validates before it
+  writes (the cache is untouched on error, as in the reference); the decode
+  kernels skip bad pages while running and the wrapper raises afterwards.
+* ``"deferred"``: no host synchronisation at all (CUDA-graph friendly); call
+  :func:`check_errors` whenever convenient to raise for any recorded error.
+"""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from . import _lib
+
+_MODES = ("sync", "deferred")
+_state = threading.local()
+_words: dict[int, torch.Tensor] = {}
+_words_lock = threading.Lock()
+
+
+def set_validation_mode(mode: str) -> None:
+    if mode not in _MODES:
+        raise ValueError(f"validation mode must be one of {_MODES}")
+    _state.mode = mode
+
+
+def validation_mode() -> str:
+    return getattr(_state, "mode", "sync")
+
+
+def error_word(device: torch.device) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    with _words_lock:
+        w = _words.get(idx)
+        if w is None:
+            w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+            _words[idx] = w
+    return w
+
+
+# bit -> (exception type, message), in the order the reference checks
+_APPEND_ERRORS = (
+    (_lib.ERR_DUP_SLOT, ValueError, "duplicate physical KV-cache slots are not allowed"),
+    (_lib.ERR_SLOT_RANGE, IndexError, "slot_mapping points outside allocated KV cache"),
+    (_lib.ERR_POS_NEGATIVE, IndexError, "positions must be non-negative"),
+    (_lib.ERR_POS_RANGE, IndexError, "positions point outside RoPE cache"),
+)
+_DECODE_ERRORS = (
+    (_lib.ERR_SEQ_LEN, ValueError, "all sequence lengths must be positive"),
+    (_lib.ERR_BLOCK_TABLE, ValueError, "block_table does not contain enough pages"),
+    (_lib.ERR_PAGE_ID, IndexError, "block_table contains an invalid physical page id"),
+)
+_ALL_ERRORS = _APPEND_ERRORS + _DECODE_ERRORS + (
+    (_lib.ERR_PIPELINE_TIMEOUT, RuntimeError, "a decode pipeline wait timed out"),)
+
+
+def raise_for_bits(bits: int) -> None:
+    for bit, exc, msg in _ALL_ERRORS:
+        if bits & bit:
+            raise exc(msg)
+    if bits:
+        raise RuntimeError(f"iris_kernel: unknown device error bits 0x{bits:x}")
+
+
+def read_and_clear(word: torch.Tensor) -> int:
+    bits = int(word.item())
+    if bits:
+        word.zero_()
+    return bits
+
+
+def check_errors(device: torch.device | int | None = None) -> None:
+    """Raise (and clear) any error the kernels recorded on ``device``."""
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    elif isinstance(device, int):
+        device = torch.device("cuda", device)
+    raise_for_bits(read_and_clear(error_word(device)))
+
+
+def require_sm100(device: torch.device) -> None:
+    cap = torch.cuda.get_device_capability(device)
+    if cap[0] != 10:
+        raise RuntimeError(f"iris_kernel is built for sm_100a (B200); device capability is {cap}")
+
+
+def stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream

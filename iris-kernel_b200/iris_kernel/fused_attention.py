@@ -1,0 +1,189 @@
+"""Read path: INT4 paged decode attention.
+
+Drop-in for ``iris_kernel.fused_attention.fused_int4_paged_decode_attention``
+of Hunter2030ZeRo/Iris-Kernel (src/iris_kernel/fused_attention.py:437-525):
+same signature, layouts, output allocation and exception types.  The work
+runs in the sm_100a kernels behind ``iris_b200_int4_paged_decode``
+(csrc/decode.cu): split-KV over all SMs plus an in-call combine.
+
+``decode_partial`` is the log-sum-exp form used by split-context multi-GPU
+decode (``iris_kernel.parallel``); it has no counterpart in the reference.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib, _runtime
+
+
+def _validate_common_decode_inputs(query, block_table, seq_lens, *, num_pages, num_kv_heads, page_size):
+    """Host-side checks of fused_attention.py:373-434 minus the data-dependent
+    ones (positive lengths, table length, page ids), which the kernels check
+    on the device (see ``_runtime``)."""
+    if not torch.cuda.is_available():
+        raise RuntimeError("Iris fused kernels require CUDA")
+    if query.device.type != "cuda":
+        raise ValueError("query must be a CUDA tensor")
+    if query.ndim != 3:
+        raise ValueError("query must have shape [B, Hq, D]")
+    if query.dtype != torch.float16:
+        raise TypeError("query must use FP16(torch.float16)")
+    if page_size != 16:
+        raise NotImplementedError("decode fast path currently supports page_size=16")
+    batch, num_query_heads, head_dim = query.shape
+    if head_dim not in (64, 128):
+        raise NotImplementedError("decode fast path currently supports head_dim in {64, 128}")
+    if num_query_heads % num_kv_heads != 0:
+        raise ValueError("num_query_heads must be divisible by num_kv_heads")
+    if num_query_heads // num_kv_heads > 16:
+        raise NotImplementedError("decode fast path supports at most 16 query heads per KV head")
+    if block_table.ndim != 2 or block_table.shape[0] != batch:
+        raise ValueError("block_table must have shape [B, max_pages_per_sequence]")
+    if seq_lens.shape != (batch,):
+        raise ValueError("seq_lens must have shape [B]")
+    if block_table.dtype != torch.int32 or seq_lens.dtype != torch.int32:
+        raise TypeError("block_table and seq_lens must use torch.int32")
+    device = query.device
+    if block_table.device != device or seq_lens.device != device:
+        raise ValueError("block_table and seq_lens must be on the query device")
+    _runtime.require_sm100(device)
+    return batch, num_query_heads, head_dim
+
+
+def _check_cache(query, k_data, v_data, k_scale, v_scale, page_size, group_size):
+    if group_size != 32:
+        raise NotImplementedError("decode fast path currently supports group_size=32")
+    if k_data.ndim != 4 or tuple(v_data.shape) != tuple(k_data.shape):
+        raise ValueError("k_data/v_data must have identical rank-4 shapes")
+    num_pages, cache_page_size, num_kv_heads, packed_dim = k_data.shape
+    head_dim = query.shape[-1]
+    if cache_page_size != page_size or packed_dim * 2 != head_dim:
+        raise ValueError("packed cache shape does not match query/page_size")
+    return num_pages, num_kv_heads, head_dim
+
+
+def _check_scales(query, k_data, v_data, k_scale, v_scale, num_pages, num_kv_heads, head_dim, page_size, group_size):
+    expected = (num_pages, page_size, num_kv_heads, head_dim // group_size)
+    if tuple(k_scale.shape) != expected:
+        raise ValueError(f"k_scale must have shape {expected}")
+    if tuple(v_scale.shape) != expected:
+        raise ValueError(f"v_scale must have shape {expected}")
+    if k_data.dtype != torch.uint8 or v_data.dtype != torch.uint8:
+        raise TypeError("k_data/v_data must use UINT8(torch.uint8)")
+    if k_scale.dtype != torch.float16 or v_scale.dtype != torch.float16:
+        raise TypeError("k_scale/v_scale must use FP16(torch.float16)")
+    for name, t in (("k_data", k_data), ("v_data", v_data), ("k_scale", k_scale), ("v_scale", v_scale)):
+        if t.device != query.device:
+            raise ValueError(f"{name} must be on {query.device}")
+    if num_pages == 0:
+        raise IndexError("block_table contains an invalid physical page id")
+    for name, t in (("query", query), ("k_data", k_data), ("v_data", v_data), ("k_scale", k_scale),
+                    ("v_scale", v_scale)):
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+
+
+def _launch(query, k_data, v_data, k_scale, v_scale, block_table, seq_lens, out, out_lse, mode, softmax_scale,
+            page_size):
+    device = query.device
+    batch, hq, head_dim = query.shape
+    num_pages, _, hkv, _ = k_data.shape
+    if block_table.stride(1) != 1 and block_table.shape[1] > 1:
+        raise ValueError("block_table rows must be contiguous")
+    scale = head_dim ** -0.5 if softmax_scale is None or softmax_scale == 0.0 else float(softmax_scale)
+    with torch.cuda.device(device):
+        stream = _runtime.stream_ptr(device)
+        word = _runtime.error_word(device)
+        if not seq_lens.is_contiguous():
+            seq_lens = seq_lens.contiguous()
+        ws_bytes = _lib.lib.iris_b200_decode_workspace_bytes(batch, hq, hkv, head_dim, device.index or 0)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
+        _lib.check_status(
+            _lib.lib.iris_b200_int4_paged_decode(
+                query.data_ptr(), k_data.data_ptr(), v_data.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(),
+                block_table.data_ptr(), block_table.stride(0), seq_lens.data_ptr(), out.data_ptr(),
+                out_lse.data_ptr() if out_lse is not None else None, mode, batch, hq, hkv, head_dim, num_pages,
+                page_size, block_table.shape[1], scale, ws.data_ptr(), ws.numel(), word.data_ptr(), stream),
+            "iris_b200_int4_paged_decode")
+        if _runtime.validation_mode() == "sync":
+            _runtime.raise_for_bits(_runtime.read_and_clear(word))
+
+
+def fused_int4_paged_decode_attention(
+    query: torch.Tensor,
+    k_data: torch.Tensor,
+    v_data: torch.Tensor,
+    k_scale: torch.Tensor,
+    v_scale: torch.Tensor,
+    block_table: torch.Tensor,
+    seq_lens: torch.Tensor,
+    output: torch.Tensor | None = None,
+    *,
+    page_size: int = 16,
+    group_size: int = 32,
+    softmax_scale: float | None = None,
+) -> torch.Tensor:
+    """
+    Fused decode attention over Iris INT4 paged K/V.
+
+    Direct path: packed load -> signed nibble unpack -> group dequantization
+    -> QK -> online softmax -> PV, FP32 accumulation, fp16 output.  No FP16
+    K/V is materialised in global memory.  ``softmax_scale`` None (or 0.0, as
+    in the reference kernel) means head_dim ** -0.5.
+    """
+    num_pages, num_kv_heads, head_dim = _check_cache(query, k_data, v_data, k_scale, v_scale, page_size, group_size)
+    _validate_common_decode_inputs(query, block_table, seq_lens, num_pages=num_pages, num_kv_heads=num_kv_heads,
+                                   page_size=page_size)
+    _check_scales(query, k_data, v_data, k_scale, v_scale, num_pages, num_kv_heads, head_dim, page_size, group_size)
+    if output is None:
+        output = torch.empty_like(query)
+    elif output.shape != query.shape or output.dtype != query.dtype:
+        raise ValueError("output must match query shape and dtype")
+    elif output.device != query.device:
+        raise ValueError("output must be on the same device as query")
+    if not output.is_contiguous():
+        raise ValueError("output must be contiguous")
+    if query.shape[0] == 0:
+        return output
+    _launch(query, k_data, v_data, k_scale, v_scale, block_table, seq_lens, output, None, _lib.DECODE_OUT_FP16,
+            softmax_scale, page_size)
+    return output
+
+
+def decode_partial(query, k_data, v_data, k_scale, v_scale, block_table, seq_lens, *, page_size: int = 16,
+                   group_size: int = 32, softmax_scale: float | None = None):
+    """Decode attention in log-sum-exp form: returns ``(o, lse)`` with
+    ``o [B, Hq, D]`` fp32 normalised over the given tokens and ``lse [B, Hq]``
+    fp32 = log2(sum_l 2^(x_l)), x_l = softmax_scale * log2(e) * q.k_l.
+    ``block_table`` may be a column slice (row stride > width) so that a
+    caller can attend over a page-aligned sub-range of each sequence."""
+    num_pages, num_kv_heads, head_dim = _check_cache(query, k_data, v_data, k_scale, v_scale, page_size, group_size)
+    _validate_common_decode_inputs(query, block_table, seq_lens, num_pages=num_pages, num_kv_heads=num_kv_heads,
+                                   page_size=page_size)
+    _check_scales(query, k_data, v_data, k_scale, v_scale, num_pages, num_kv_heads, head_dim, page_size, group_size)
+    out = torch.empty(query.shape, dtype=torch.float32, device=query.device)
+    lse = torch.empty(query.shape[:2], dtype=torch.float32, device=query.device)
+    if query.shape[0]:
+        _launch(query, k_data, v_data, k_scale, v_scale, block_table, seq_lens, out, lse, _lib.DECODE_OUT_LSE,
+                softmax_scale, page_size)
+    return out, lse
+
+
+def merge_lse_partials(parts_o: torch.Tensor, parts_lse: torch.Tensor, output: torch.Tensor | None = None):
+    """Merge ``parts_o [P, B, Hq, D]`` / ``parts_lse [P, B, Hq]`` (as returned
+    by :func:`decode_partial` for disjoint token ranges) into fp16 output."""
+    if parts_o.dtype != torch.float32 or parts_lse.dtype != torch.float32:
+        raise TypeError("partials must be float32")
+    if parts_o.ndim != 4 or parts_lse.shape != parts_o.shape[:3]:
+        raise ValueError("parts_o must be [P, B, Hq, D] and parts_lse [P, B, Hq]")
+    P, B, Hq, D = parts_o.shape
+    if output is None:
+        output = torch.empty((B, Hq, D), dtype=torch.float16, device=parts_o.device)
+    parts_o = parts_o.contiguous()
+    parts_lse = parts_lse.contiguous()
+    with torch.cuda.device(parts_o.device):
+        _lib.check_status(
+            _lib.lib.iris_b200_merge_lse_partials(parts_o.data_ptr(), parts_lse.data_ptr(), P, B * Hq, D,
+                                                  output.data_ptr(), _runtime.stream_ptr(parts_o.device)),
+            "iris_b200_merge_lse_partials")
+    return output

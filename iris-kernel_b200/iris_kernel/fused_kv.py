@@ -1,0 +1,142 @@
+"""Write path: fused RoPE(K) + INT4 quantise + pack + paged append.
+
+Drop-in for ``iris_kernel.fused_kv.fused_rope_int4_paged_append`` of
+Hunter2030ZeRo/Iris-Kernel (src/iris_kernel/fused_kv.py:600-780): same
+signature, tensor layouts and exception types.  The work runs in the sm_100a
+kernel ``iris_b200_rope_int4_paged_append`` (csrc/append.cu) and is
+bit-exact with the reference's eager path (torch_eager_kv.py:110-337).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib, _runtime
+
+
+def _check_append_args(key, value, positions, slot_mapping, cos_cache, sin_cache, k_data, v_data, k_scale, v_scale,
+                       *, rotary_dim, group_size, page_size):
+    """Host-side argument checks, in the order of fused_kv.py:616-739."""
+    if key.device.type != "cuda":
+        raise ValueError("key/value must be CUDA tensors")
+    if key.shape != value.shape:
+        raise ValueError("key and value must have identical shapes")
+    if key.ndim != 3:
+        raise ValueError("key/value must have shape [T, Hkv, D]")
+    if key.dtype != torch.float16:
+        raise TypeError("key must use FP16(torch.float16)")
+    if value.dtype != torch.float16:
+        raise TypeError("value must use FP16(torch.float16)")
+    num_tokens, num_kv_heads, head_dim = key.shape
+    if head_dim % 64 != 0:
+        raise NotImplementedError("fused append requires head_dim divisible by 64")
+    if head_dim > 512:
+        raise NotImplementedError("fused append supports head_dim <= 512")
+    if group_size != 32:
+        raise NotImplementedError("fused append supports group_size=32")
+    if rotary_dim != head_dim:
+        raise NotImplementedError("fused append requires rotary_dim == head_dim")
+    if rotary_dim % 2 != 0:
+        raise ValueError("rotary_dim must be even")
+    if page_size <= 0:
+        raise ValueError("page_size must be positive")
+    if positions.shape != (num_tokens,):
+        raise ValueError("positions must have shape [T]")
+    if slot_mapping.shape != (num_tokens,):
+        raise ValueError("slot_mapping must have shape [T]")
+    device = key.device
+    for name, t in (("value", value), ("positions", positions), ("slot_mapping", slot_mapping),
+                    ("cos_cache", cos_cache), ("sin_cache", sin_cache), ("k_data", k_data), ("v_data", v_data),
+                    ("k_scale", k_scale), ("v_scale", v_scale)):
+        if t.device != device:
+            raise ValueError(f"{name} must be on {device}")
+    if positions.dtype != torch.int32:
+        raise TypeError("positions must use torch.int32")
+    if slot_mapping.dtype != torch.int32:
+        raise TypeError("slot_mapping must use torch.int32")
+    half = rotary_dim // 2
+    if cos_cache.ndim != 2:
+        raise ValueError("cos_cache must have shape [max_position, rotary_dim // 2]")
+    if sin_cache.shape != cos_cache.shape:
+        raise ValueError("sin_cache must match cos_cache")
+    if cos_cache.shape[-1] != half:
+        raise ValueError(f"RoPE cache width must be {half}")
+    if cos_cache.dtype != torch.float16:
+        raise TypeError("cos_cache must use FP16(torch.float16)")
+    if sin_cache.dtype != torch.float16:
+        raise TypeError("sin_cache must use FP16(torch.float16)")
+    if k_data.ndim != 4:
+        raise ValueError("k_data/v_data must be rank-4 tensors")
+    num_pages = k_data.shape[0]
+    data_shape = (num_pages, page_size, num_kv_heads, head_dim // 2)
+    scale_shape = (num_pages, page_size, num_kv_heads, head_dim // group_size)
+    if tuple(k_data.shape) != data_shape:
+        raise ValueError(f"k_data must have shape {data_shape}")
+    if tuple(v_data.shape) != data_shape:
+        raise ValueError(f"v_data must have shape {data_shape}")
+    if tuple(k_scale.shape) != scale_shape:
+        raise ValueError(f"k_scale must have shape {scale_shape}")
+    if tuple(v_scale.shape) != scale_shape:
+        raise ValueError(f"v_scale must have shape {scale_shape}")
+    if k_data.dtype != torch.uint8:
+        raise TypeError("k_data must use UINT8(torch.uint8)")
+    if v_data.dtype != torch.uint8:
+        raise TypeError("v_data must use UINT8(torch.uint8)")
+    if k_scale.dtype != torch.float16:
+        raise TypeError("k_scale must use FP16(torch.float16)")
+    if v_scale.dtype != torch.float16:
+        raise TypeError("v_scale must use FP16(torch.float16)")
+    for name, t in (("key", key), ("value", value), ("positions", positions), ("slot_mapping", slot_mapping),
+                    ("cos_cache", cos_cache), ("sin_cache", sin_cache), ("k_data", k_data), ("v_data", v_data),
+                    ("k_scale", k_scale), ("v_scale", v_scale)):
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    return num_tokens, num_kv_heads, head_dim, num_pages
+
+
+def fused_rope_int4_paged_append(
+    key: torch.Tensor,
+    value: torch.Tensor,
+    positions: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    cos_cache: torch.Tensor,
+    sin_cache: torch.Tensor,
+    k_data: torch.Tensor,
+    v_data: torch.Tensor,
+    k_scale: torch.Tensor,
+    v_scale: torch.Tensor,
+    *,
+    rotary_dim: int,
+    group_size: int = 32,
+    page_size: int,
+) -> None:
+    """RoPE(K), group-32 INT4 quantisation of K and V, low-nibble-first
+    packing and paged append, in place.  Tokens with ``slot_mapping < 0`` are
+    skipped; untouched slots stay byte-identical."""
+    if not torch.cuda.is_available():
+        raise RuntimeError("Iris fused kernels require CUDA")
+    num_tokens, num_kv_heads, head_dim, num_pages = _check_append_args(
+        key, value, positions, slot_mapping, cos_cache, sin_cache, k_data, v_data, k_scale, v_scale,
+        rotary_dim=rotary_dim, group_size=group_size, page_size=page_size)
+    device = key.device
+    _runtime.require_sm100(device)
+    if num_tokens == 0:
+        return
+    with torch.cuda.device(device):
+        stream = _runtime.stream_ptr(device)
+        word = _runtime.error_word(device)
+        ws_bytes = _lib.lib.iris_b200_append_check_workspace_bytes(num_pages, page_size)
+        ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=device)
+        _lib.check_status(
+            _lib.lib.iris_b200_append_check(positions.data_ptr(), slot_mapping.data_ptr(), num_tokens,
+                                            cos_cache.shape[0], num_pages, page_size, ws.data_ptr(), ws.numel(),
+                                            word.data_ptr(), stream),
+            "iris_b200_append_check")
+        if _runtime.validation_mode() == "sync":
+            _runtime.raise_for_bits(_runtime.read_and_clear(word))
+        _lib.check_status(
+            _lib.lib.iris_b200_rope_int4_paged_append(
+                key.data_ptr(), value.data_ptr(), positions.data_ptr(), slot_mapping.data_ptr(),
+                cos_cache.data_ptr(), sin_cache.data_ptr(), k_data.data_ptr(), v_data.data_ptr(),
+                k_scale.data_ptr(), v_scale.data_ptr(), num_tokens, num_kv_heads, head_dim, cos_cache.shape[0],
+                num_pages, page_size, word.data_ptr(), stream),
+            "iris_b200_rope_int4_paged_append")
