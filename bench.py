@@ -92,22 +92,26 @@ class Clocks:
     def __enter__(self):
         try:
             os.makedirs(os.path.dirname(self.path), exist_ok=True)
-            self.f = open(self.path, "w")
+            if os.path.exists(self.path):
+                os.remove(self.path)
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f,
-                                         stderr=subprocess.DEVNULL)
+                                          "--format=csv,noheader,nounits", "-lms", "50", "-f", self.path],
+                                         stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+            t0 = time.time()  # start timing only once samples are flowing
+            while time.time() - t0 < 10 and (not os.path.exists(self.path) or os.path.getsize(self.path) == 0):
+                time.sleep(0.05)
         except Exception:
             self.proc = None
         return self
 
     def __exit__(self, *a):
         if self.proc is not None:
+            time.sleep(0.2)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
-            self.f.close()
 
     def summary(self):
         if self.proc is None:
@@ -298,7 +302,7 @@ def _config():
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -324,10 +328,10 @@ def main():
     g_step = graph_of(lambda: (step_decode(w), step_append(w)), dev)
     g_dec = graph_of(lambda: step_decode(w), dev)
     g_app = graph_of(lambda: step_append(w), dev)
-    with Clocks(local) as clk:
-        ms = timed(g_step.replay, args.steps, dev, dist, args.warmup)
-        ms_dec = timed(g_dec.replay, args.steps, dev, dist, args.warmup)
-        ms_app = timed(g_app.replay, args.steps, dev, dist, args.warmup)
+    clk = Clocks(local).__enter__()
+    ms = timed(g_step.replay, args.steps, dev, dist, args.warmup)
+    ms_dec = timed(g_dec.replay, args.steps, dev, dist, args.warmup)
+    ms_app = timed(g_app.replay, args.steps, dev, dist, args.warmup)
     iris_kernel.check_errors(dev)
     iris_kernel.set_validation_mode("sync")
     ms = max_over_ranks(ms, dist, dev)
@@ -365,6 +369,7 @@ def main():
         hout.copy_(out, non_blocking=True)
 
     ms_e2e = timed(e2e_step, args.steps, dev, dist, args.warmup)
+    clk.__exit__(None, None, None)
     ms_e2e = max_over_ranks(ms_e2e, dist, dev)
     e2e_value = world * STEP_BYTES / (ms_e2e / args.steps * 1e-3) / 1e12
 

@@ -16,10 +16,19 @@
 
 namespace iris {
 
-// Bounded spin: ~2^26 polls of try_wait (each poll may itself suspend for a
-// hardware-chosen interval), i.e. seconds.  On expiry the waiter records
-// IRIS_ERR_PIPELINE_TIMEOUT and gives up instead of hanging the GPU.
-constexpr uint32_t kMaxPolls = 1u << 26;
+// Bounded waits.  Each poll is an mbarrier.try_wait with a suspend-time
+// hint, so a waiting warp sleeps in hardware (no issue slots burnt) until the
+// phase completes or the hint expires.  A wait gives up after kWaitLimitNs of
+// %globaltimer time (whatever the hardware does with the hint), records
+// IRIS_ERR_PIPELINE_TIMEOUT and returns instead of hanging the GPU.
+constexpr uint32_t kSuspendHintNs = 100000;        // 0.1 ms per poll at most
+constexpr uint64_t kWaitLimitNs = 2000000000ull;   // 2 s per wait
+
+IRIS_DEV uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 IRIS_DEV void set_error(int32_t* err, int32_t bits) {
   if (err != nullptr) atomicOr(err, bits);
@@ -51,23 +60,46 @@ IRIS_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
       : "memory");
 }
 
-IRIS_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+IRIS_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
 
 // Returns false (and records the timeout) if the phase never completes.
-IRIS_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int32_t* err) {
-  for (uint32_t i = 0; i < kMaxPolls; ++i) {
+IRIS_DEV bool mbar_wait_bounded(uint32_t bar, uint32_t parity, int32_t* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) break;
   }
   set_error(err, IRIS_ERR_PIPELINE_TIMEOUT);
   return false;
+}
+
+IRIS_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int32_t* err) {
+  return mbar_wait_bounded(smem_u32(bar), parity, err);
+}
+
+IRIS_DEV void mbar_arrive(uint32_t bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar) : "memory");
+}
+
+IRIS_DEV uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+
+IRIS_DEV uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
 }
 
 // --------------------------------------------------------------- TMA copies

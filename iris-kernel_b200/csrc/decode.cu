@@ -232,13 +232,16 @@ IRIS_DEV uint32_t tile_lane_offset(int lane, int i) {
 }
 
 // One page (16 tokens) of one KV head.
+// Scores of one page (16 tokens) for this warp's KV head:
+// s[nt][0..3] = S^T[token g8 / g8+8][query head 2t / 2t+1] (unscaled logits).
+// ktile / ksc are shared-memory addresses of the head's K tile and of its
+// column in the page's K scale block (row stride `scale_stride` bytes).
 template <int D, int NT>
-IRIS_DEV void process_page(WarpState<D, NT>& st, uint32_t ktile, uint32_t vtile, const __half* __restrict__ ksc,
-                           const __half* __restrict__ vsc, int scale_stride, int valid, float scale_log2, int lane) {
+IRIS_DEV void page_scores(const WarpState<D, NT>& st, uint32_t ktile, uint32_t ksc, int scale_stride, int lane,
+                          float (&s)[NT][4]) {
   constexpr int G = D / 32;
-  const int g8 = lane >> 2, t = lane & 3;
-
-  // ---- K fragments: kw[grp][0] = token g8, kw[grp][1] = token g8 + 8 ----
+  const int g8 = lane >> 2;
+  // kw[grp][0] = token g8, kw[grp][1] = token g8 + 8 (32 dims of group grp)
   uint32_t kw[G][2];
 #pragma unroll
   for (int i = 0; i < G / 2; ++i) {
@@ -249,28 +252,21 @@ IRIS_DEV void process_page(WarpState<D, NT>& st, uint32_t ktile, uint32_t vtile,
     kw[2 * i + 1][0] = r[2];
     kw[2 * i + 1][1] = r[3];
   }
-
-  // K scales of this lane's two token rows
   float ks[2][G];
 #pragma unroll
   for (int rr = 0; rr < 2; ++rr) {
-    const __half* sp = ksc + (g8 + 8 * rr) * scale_stride;
+    const uint32_t sp = ksc + (g8 + 8 * rr) * scale_stride;
     if constexpr (G == 4) {
-      const uint2 u = *reinterpret_cast<const uint2*>(sp);
+      const uint2 u = lds64(sp);
       const float2 a = __half22float2(u32_as_h2(u.x)), b = __half22float2(u32_as_h2(u.y));
       ks[rr][0] = a.x; ks[rr][1] = a.y; ks[rr][2] = b.x; ks[rr][3] = b.y;
     } else {
-      const float2 a = __half22float2(u32_as_h2(*reinterpret_cast<const uint32_t*>(sp)));
+      const float2 a = __half22float2(u32_as_h2(lds32(sp)));
       ks[rr][0] = a.x; ks[rr][1] = a.y;
     }
   }
-
-  const bool row0_ok = g8 < valid, row1_ok = (g8 + 8) < valid;
-
-  float p[NT][4];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
-    float s[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       float acc[4] = {-st.corr[nt][g][0], -st.corr[nt][g][1], -st.corr[nt][g][0], -st.corr[nt][g][1]};
@@ -280,61 +276,44 @@ IRIS_DEV void process_page(WarpState<D, NT>& st, uint32_t ktile, uint32_t vtile,
         const uint32_t a[4] = {int4_lo_biased(w0), int4_lo_biased(w1), int4_hi_biased(w0), int4_hi_biased(w1)};
         mma_16816(acc, a, st.qf[nt][2 * g + sub][0], st.qf[nt][2 * g + sub][1], acc);
       }
-      s[0] = fmaf(ks[0][g], acc[0], s[0]);
-      s[1] = fmaf(ks[0][g], acc[1], s[1]);
-      s[2] = fmaf(ks[1][g], acc[2], s[2]);
-      s[3] = fmaf(ks[1][g], acc[3], s[3]);
-    }
-    // scaled logits, tail tokens masked
-    float x0 = row0_ok ? s[0] * scale_log2 : kNegInf;
-    float x1 = row0_ok ? s[1] * scale_log2 : kNegInf;
-    float x2 = row1_ok ? s[2] * scale_log2 : kNegInf;
-    float x3 = row1_ok ? s[3] * scale_log2 : kNegInf;
-    float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-    }
-    const float mn0 = fmaxf(st.m[nt][0], mx0), mn1 = fmaxf(st.m[nt][1], mx1);
-    const bool grow = (mn0 > st.m[nt][0]) || (mn1 > st.m[nt][1]);
-    if (__any_sync(0xffffffffu, grow)) {
-      const float c0 = ex2(st.m[nt][0] - mn0), c1 = ex2(st.m[nt][1] - mn1);  // ex2(-inf) = 0
-#pragma unroll
-      for (int i = 0; i < D / 16; ++i) {
-        st.o[nt][i][0] *= c0;
-        st.o[nt][i][1] *= c1;
-        st.o[nt][i][2] *= c0;
-        st.o[nt][i][3] *= c1;
+      if (g == 0) {
+        s[nt][0] = ks[0][g] * acc[0];
+        s[nt][1] = ks[0][g] * acc[1];
+        s[nt][2] = ks[1][g] * acc[2];
+        s[nt][3] = ks[1][g] * acc[3];
+      } else {
+        s[nt][0] = fmaf(ks[0][g], acc[0], s[nt][0]);
+        s[nt][1] = fmaf(ks[0][g], acc[1], s[nt][1]);
+        s[nt][2] = fmaf(ks[1][g], acc[2], s[nt][2]);
+        s[nt][3] = fmaf(ks[1][g], acc[3], s[nt][3]);
       }
-      st.l[nt][0] *= c0;
-      st.l[nt][1] *= c1;
-      st.m[nt][0] = mn0;
-      st.m[nt][1] = mn1;
     }
-    p[nt][0] = ex2(x0 - st.m[nt][0]);
-    p[nt][1] = ex2(x1 - st.m[nt][1]);
-    p[nt][2] = ex2(x2 - st.m[nt][0]);
-    p[nt][3] = ex2(x3 - st.m[nt][1]);
-    st.l[nt][0] += p[nt][0] + p[nt][2];
-    st.l[nt][1] += p[nt][1] + p[nt][3];
   }
+}
 
-  // ---- V scales for tokens 2t, 2t+1, 2t+8, 2t+9, zeroed past the tail ----
-  uint32_t sv01[G], sv89[G];  // half2 (token a, token b) per group
+// O += V^T P'^T for one page.  p[nt][0..3] are this lane's probabilities in
+// the score layout; tokens >= `valid` get a zero V scale when MASK (their
+// slots may hold garbage, even NaN scales).
+template <int D, int NT, bool MASK>
+IRIS_DEV void page_pv(WarpState<D, NT>& st, uint32_t vtile, uint32_t vsc, int scale_stride, int valid,
+                      const float (&p)[NT][4], int lane) {
+  constexpr int G = D / 32;
+  const int t = lane & 3;
+  // V scales of tokens 2t, 2t+1, 2t+8, 2t+9 as half2 (token a, token b) per group
+  uint32_t sv01[G], sv89[G];
   {
     uint32_t raw[4][G / 2];
-    const int toks[4] = {2 * t, 2 * t + 1, 2 * t + 8, 2 * t + 9};
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const __half* sp = vsc + toks[k] * scale_stride;
-      const bool ok = toks[k] < valid;
+      const int tok = 2 * t + (k & 1) + 8 * (k >> 1);
+      const uint32_t sp = vsc + tok * scale_stride;
+      const bool ok = !MASK || tok < valid;
       if constexpr (G == 4) {
-        uint2 u = *reinterpret_cast<const uint2*>(sp);
+        const uint2 u = lds64(sp);
         raw[k][0] = ok ? u.x : 0u;
         raw[k][1] = ok ? u.y : 0u;
       } else {
-        const uint32_t u = *reinterpret_cast<const uint32_t*>(sp);
+        const uint32_t u = lds32(sp);
         raw[k][0] = ok ? u : 0u;
       }
     }
@@ -346,16 +325,13 @@ IRIS_DEV void process_page(WarpState<D, NT>& st, uint32_t ktile, uint32_t vtile,
       sv89[2 * j + 1] = prmt(raw[2][j], raw[3][j], 0x7632);
     }
   }
-
-  // ---- P^T as B operands (one per group: P scaled by that group's V scale) ----
+  // P^T as B operands via an in-register 8x8 transpose
   uint32_t pb[NT][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     pb[nt][0] = movmatrix_trans(h2_as_u32(__floats2half2_rn(p[nt][0], p[nt][1])));
     pb[nt][1] = movmatrix_trans(h2_as_u32(__floats2half2_rn(p[nt][2], p[nt][3])));
   }
-
-  // ---- V fragments and PV ----
 #pragma unroll
   for (int i = 0; i < G / 2; ++i) {
     uint32_t r[4];
@@ -381,6 +357,71 @@ IRIS_DEV void process_page(WarpState<D, NT>& st, uint32_t ktile, uint32_t vtile,
       }
     }
   }
+}
+
+// NPG consecutive pages (1 or 2) of this warp's KV head with one online-
+// softmax update.  base[i] is the shared address of page i's stage; `valid`
+// counts the sequence's tokens from page 0 on (MASK: fewer than 16*NPG).
+template <int D, int NT, int NPG, bool MASK>
+IRIS_DEV void process_pages(WarpState<D, NT>& st, const uint32_t (&base)[NPG], uint32_t k_off, uint32_t v_off,
+                            uint32_t ks_off, uint32_t vs_off, int scale_stride, int valid, float scale_log2,
+                            int lane) {
+  const int g8 = lane >> 2;
+  float x[NPG][NT][4];
+#pragma unroll
+  for (int pi = 0; pi < NPG; ++pi) {
+    page_scores<D, NT>(st, base[pi] + k_off, base[pi] + ks_off, scale_stride, lane, x[pi]);
+    const bool r0 = !MASK || g8 + 16 * pi < valid, r1 = !MASK || g8 + 8 + 16 * pi < valid;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      x[pi][nt][0] = r0 ? x[pi][nt][0] * scale_log2 : kNegInf;
+      x[pi][nt][1] = r0 ? x[pi][nt][1] * scale_log2 : kNegInf;
+      x[pi][nt][2] = r1 ? x[pi][nt][2] * scale_log2 : kNegInf;
+      x[pi][nt][3] = r1 ? x[pi][nt][3] * scale_log2 : kNegInf;
+    }
+  }
+  float p[NPG][NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    float mx0 = fmaxf(x[0][nt][0], x[0][nt][2]), mx1 = fmaxf(x[0][nt][1], x[0][nt][3]);
+#pragma unroll
+    for (int pi = 1; pi < NPG; ++pi) {
+      mx0 = fmaxf(mx0, fmaxf(x[pi][nt][0], x[pi][nt][2]));
+      mx1 = fmaxf(mx1, fmaxf(x[pi][nt][1], x[pi][nt][3]));
+    }
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+    }
+    const float mn0 = fmaxf(st.m[nt][0], mx0), mn1 = fmaxf(st.m[nt][1], mx1);
+    if (__any_sync(0xffffffffu, (mn0 > st.m[nt][0]) || (mn1 > st.m[nt][1]))) {
+      const float c0 = ex2(st.m[nt][0] - mn0), c1 = ex2(st.m[nt][1] - mn1);  // ex2(-inf) = 0
+#pragma unroll
+      for (int i = 0; i < D / 16; ++i) {
+        st.o[nt][i][0] *= c0;
+        st.o[nt][i][1] *= c1;
+        st.o[nt][i][2] *= c0;
+        st.o[nt][i][3] *= c1;
+      }
+      st.l[nt][0] *= c0;
+      st.l[nt][1] *= c1;
+      st.m[nt][0] = mn0;
+      st.m[nt][1] = mn1;
+    }
+#pragma unroll
+    for (int pi = 0; pi < NPG; ++pi) {
+      p[pi][nt][0] = ex2(x[pi][nt][0] - st.m[nt][0]);
+      p[pi][nt][1] = ex2(x[pi][nt][1] - st.m[nt][1]);
+      p[pi][nt][2] = ex2(x[pi][nt][2] - st.m[nt][0]);
+      p[pi][nt][3] = ex2(x[pi][nt][3] - st.m[nt][1]);
+      st.l[nt][0] += p[pi][nt][0] + p[pi][nt][2];
+      st.l[nt][1] += p[pi][nt][1] + p[pi][nt][3];
+    }
+  }
+#pragma unroll
+  for (int pi = 0; pi < NPG; ++pi)
+    page_pv<D, NT, MASK>(st, base[pi] + v_off, base[pi] + vs_off, scale_stride, valid - 16 * pi, p[pi], lane);
 }
 
 // Finish a (sequence piece, KV head): reduce l over the lane's token rows,
@@ -436,7 +477,7 @@ IRIS_DEV void finish_piece(const DecodeParams& p, WarpState<D, NT>& st, int b, i
 }
 
 template <int D, int NT>
-__global__ void __launch_bounds__(9 * 32) decode_kernel(const __grid_constant__ CUtensorMap kmap,
+__global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ CUtensorMap kmap,
                                                         const __grid_constant__ CUtensorMap vmap,
                                                         const DecodeParams p) {
   using C = DecCfg<D>;
@@ -467,49 +508,79 @@ __global__ void __launch_bounds__(9 * 32) decode_kernel(const __grid_constant__ 
 
   const int64_t u0 = range_start(r, U, R), u1 = range_start(r + 1, U, R);
   const int b_first = p.range_seq[r];
+  const uint32_t full_u32 = smem_u32(full), empty_u32 = smem_u32(empty);
 
   if (warp == HB) {
     // ======================= producer warp =======================
+    // All lanes fetch (and validate) page ids 32 at a time, one chunk ahead
+    // of lane 0, which waits for free stages and issues the copies.
     if (lane == 0) {
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
-      const uint32_t tx = 2 * HB * C::kTileBytes + 2 * scale_block;
-      uint32_t it = 0;
-      bool alive = true;
-      int b = b_first;
-      int64_t u = u0;
-      while (alive && u < u1) {
-        const int64_t ps = p.prefix[b], pe = p.prefix[b + 1];
-        if (pe <= u) { ++b; continue; }
-        const int64_t hi = pe < u1 ? pe : u1;
-        const int32_t* bt_row = p.block_table + static_cast<int64_t>(b) * p.bt_stride;
-        for (int64_t pg = u; pg < hi; ++pg, ++it) {
-          const int s = it % S;
-          const uint32_t ph = (it / S) & 1;
-          if (!mbar_wait_bounded(empty + s, ph ^ 1, p.err)) { alive = false; break; }
-          int32_t pid = bt_row[pg - ps];
-          if (pid < 0 || static_cast<int64_t>(pid) >= p.num_pages) {
-            set_error(p.err, IRIS_ERR_PAGE_ID);
-            pid = 0;
-          }
-          uint8_t* st = smem + s * stage_bytes;
-          mbar_arrive_expect_tx(full + s, tx);
-          for (int h = 0; h < HB; ++h) {
-            const int kvh = hblk * HB + h;
-            tma_load_3d(st + h * C::kTileBytes, &kmap, 0, kvh, pid * kPage, full + s);
-            tma_load_3d(st + (HB + h) * C::kTileBytes, &vmap, 0, kvh, pid * kPage, full + s);
-          }
-          uint8_t* sc = st + 2 * HB * C::kTileBytes;
-          bulk_g2s(sc, p.k_scale + static_cast<int64_t>(pid) * scale_block, scale_block, full + s);
-          bulk_g2s(sc + scale_block, p.v_scale + static_cast<int64_t>(pid) * scale_block, scale_block, full + s);
+    }
+    const uint32_t tx = 2 * HB * C::kTileBytes + 2 * scale_block;
+    uint32_t issued = 0;
+    int s = 0;          // stage of the next page
+    uint32_t ph = 0;    // its ring pass parity
+    bool alive = true;
+    int b = b_first;
+    int64_t u = u0;
+    auto fetch_ids = [&](const int32_t* row, int64_t first, int64_t count) -> int32_t {
+      int32_t pid = 0;
+      if (lane < count) {
+        pid = row[first + lane];
+        if (pid < 0 || static_cast<int64_t>(pid) >= p.num_pages) {
+          set_error(p.err, IRIS_ERR_PAGE_ID);
+          pid = 0;  // stay in bounds; the error word makes the call fail
         }
-        u = hi;
-        ++b;
       }
-      // drain: every copy this CTA issued has landed before it exits
-      const uint32_t last = it;
+      return pid;
+    };
+    while (alive && u < u1) {
+      const int64_t ps = p.prefix[b], pe = p.prefix[b + 1];
+      if (pe <= u) { ++b; continue; }
+      const int64_t hi = pe < u1 ? pe : u1;
+      const int32_t* bt_row = p.block_table + static_cast<int64_t>(b) * p.bt_stride;
+      int64_t chunk = u;
+      int32_t ids = fetch_ids(bt_row, chunk - ps, hi - chunk);
+      while (chunk < hi) {
+        const int n = static_cast<int>(hi - chunk < 32 ? hi - chunk : 32);
+        const int64_t next = chunk + n;
+        const int32_t ids_next = next < hi ? fetch_ids(bt_row, next - ps, hi - next) : 0;
+        for (int j = 0; j < n; ++j) {
+          const int32_t pid = __shfl_sync(0xffffffffu, ids, j);
+          if (lane == 0 && alive) {
+            if (!mbar_wait_bounded(empty_u32 + 8 * s, ph ^ 1, p.err)) {
+              alive = false;
+            } else {
+              uint8_t* st = smem + s * stage_bytes;
+              mbar_arrive_expect_tx(full + s, tx);
+              for (int h = 0; h < HB; ++h) {
+                const int kvh = hblk * HB + h;
+                tma_load_3d(st + h * C::kTileBytes, &kmap, 0, kvh, pid * kPage, full + s);
+                tma_load_3d(st + (HB + h) * C::kTileBytes, &vmap, 0, kvh, pid * kPage, full + s);
+              }
+              uint8_t* sc = st + 2 * HB * C::kTileBytes;
+              bulk_g2s(sc, p.k_scale + static_cast<int64_t>(pid) * scale_block, scale_block, full + s);
+              bulk_g2s(sc + scale_block, p.v_scale + static_cast<int64_t>(pid) * scale_block, scale_block, full + s);
+              ++issued;
+            }
+          }
+          if (++s == S) { s = 0; ph ^= 1; }
+        }
+        alive = __shfl_sync(0xffffffffu, alive, 0);
+        if (!alive) break;
+        ids = ids_next;
+        chunk = next;
+      }
+      u = hi;
+      ++b;
+    }
+    // drain: every copy this CTA issued has landed before it exits
+    if (lane == 0) {
+      const uint32_t last = issued;  // stages are issued in order, so the last S are [issued - S, issued)
       const uint32_t first = last > static_cast<uint32_t>(S) ? last - S : 0;
-      for (uint32_t k = first; k < last; ++k) mbar_wait_bounded(full + (k % S), (k / S) & 1, p.err);
+      for (uint32_t k = first; k < last; ++k) mbar_wait_bounded(full_u32 + 8 * (k % S), (k / S) & 1, p.err);
     }
     return;
   }
@@ -517,8 +588,15 @@ __global__ void __launch_bounds__(9 * 32) decode_kernel(const __grid_constant__ 
   // ========================= consumer warps =========================
   const int kvh = hblk * HB + warp;
   WarpState<D, NT> st;
-  const uint32_t smem_base = smem_u32(smem);
-  uint32_t it = 0;
+  const uint32_t ring = smem_u32(smem);
+  // this warp's tiles and scale columns, relative to a stage's base
+  const uint32_t k_off = warp * C::kTileBytes, v_off = (HB + warp) * C::kTileBytes;
+  const uint32_t ks_off = 2 * HB * C::kTileBytes + kvh * C::kGroups * 2;
+  const uint32_t vs_off = ks_off + scale_block;
+  const int scale_stride = p.hkv * C::kGroups * 2;
+  int s = 0;
+  uint32_t ph = 0;
+  uint32_t stage = ring;  // base address of stage s
   int b = b_first;
   int64_t u = u0;
   while (u < u1) {
@@ -527,22 +605,59 @@ __global__ void __launch_bounds__(9 * 32) decode_kernel(const __grid_constant__ 
     const int64_t hi = pe < u1 ? pe : u1;
     const int L = min(p.seq_lens[b], p.max_pages * kPage);
     load_query<D, NT>(st, p.query + (static_cast<int64_t>(b) * p.hq + kvh * p.qpk) * D, p.qpk, lane);
-    bool alive = true;
-    for (int64_t pg = u; pg < hi; ++pg, ++it) {
-      const int s = it % S;
-      const uint32_t ph = (it / S) & 1;
-      if (!mbar_wait_bounded(full + s, ph, p.err)) { alive = false; break; }
-      const uint32_t stb = smem_base + s * stage_bytes;
-      const uint8_t* sc = smem + s * stage_bytes + 2 * HB * C::kTileBytes;
-      const int valid = L - static_cast<int>(pg - ps) * kPage;
-      process_page<D, NT>(st, stb + warp * C::kTileBytes, stb + (HB + warp) * C::kTileBytes,
-                          reinterpret_cast<const __half*>(sc) + kvh * C::kGroups,
-                          reinterpret_cast<const __half*>(sc + scale_block) + kvh * C::kGroups,
-                          p.hkv * C::kGroups, valid < kPage ? valid : kPage, p.scale_log2, lane);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty + s);
+    int valid = L - static_cast<int>(u - ps) * kPage;  // tokens left from this page on
+    int left = static_cast<int>(hi - u);                 // pages of this piece still to do
+    while (left > 0) {
+      // two pages per softmax update where the registers allow it (NT == 1)
+      if (NT == 1 && left >= 2) {
+        const int s1 = s + 1 == S ? 0 : s + 1;
+        const uint32_t ph1 = s + 1 == S ? ph ^ 1 : ph;
+        const uint32_t base[2] = {stage, s1 == 0 ? ring : stage + stage_bytes};
+        if (!mbar_wait_bounded(full_u32 + 8 * s, ph, p.err)) return;
+        if (!mbar_wait_bounded(full_u32 + 8 * s1, ph1, p.err)) return;
+        if (valid >= 2 * kPage)
+          process_pages<D, NT, 2, false>(st, base, k_off, v_off, ks_off, vs_off, scale_stride, valid, p.scale_log2,
+                                         lane);
+        else
+          process_pages<D, NT, 2, true>(st, base, k_off, v_off, ks_off, vs_off, scale_stride, valid, p.scale_log2,
+                                        lane);
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(empty_u32 + 8 * s);
+          mbar_arrive(empty_u32 + 8 * s1);
+        }
+        valid -= 2 * kPage;
+        left -= 2;
+        if (s1 + 1 == S) {
+          s = 0;
+          stage = ring;
+        } else {
+          s = s1 + 1;
+          stage = base[1] + stage_bytes;
+        }
+        ph = (s1 + 1 == S) ? ph1 ^ 1 : ph1;
+      } else {
+        const uint32_t base[1] = {stage};
+        if (!mbar_wait_bounded(full_u32 + 8 * s, ph, p.err)) return;
+        if (valid >= kPage)
+          process_pages<D, NT, 1, false>(st, base, k_off, v_off, ks_off, vs_off, scale_stride, valid, p.scale_log2,
+                                         lane);
+        else
+          process_pages<D, NT, 1, true>(st, base, k_off, v_off, ks_off, vs_off, scale_stride, valid, p.scale_log2,
+                                        lane);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty_u32 + 8 * s);
+        valid -= kPage;
+        left -= 1;
+        if (++s == S) {
+          s = 0;
+          ph ^= 1;
+          stage = ring;
+        } else {
+          stage += stage_bytes;
+        }
+      }
     }
-    if (!alive) return;
     const bool complete = (ps >= u0) && (pe <= u1);
     const int64_t rec = static_cast<int64_t>(r) * 2 + (u == u0 ? 0 : 1);
     finish_piece<D, NT>(p, st, b, kvh, complete, rec, lane);
