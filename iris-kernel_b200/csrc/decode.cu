@@ -555,11 +555,8 @@ __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ CUtensorM
             } else {
               uint8_t* st = smem + s * stage_bytes;
               mbar_arrive_expect_tx(full + s, tx);
-              for (int h = 0; h < HB; ++h) {
-                const int kvh = hblk * HB + h;
-                tma_load_3d(st + h * C::kTileBytes, &kmap, 0, kvh, pid * kPage, full + s);
-                tma_load_3d(st + (HB + h) * C::kTileBytes, &vmap, 0, kvh, pid * kPage, full + s);
-              }
+              tma_load_4d(st, &kmap, 0, 0, hblk * HB, pid, full + s);
+              tma_load_4d(st + HB * C::kTileBytes, &vmap, 0, 0, hblk * HB, pid, full + s);
               uint8_t* sc = st + 2 * HB * C::kTileBytes;
               bulk_g2s(sc, p.k_scale + static_cast<int64_t>(pid) * scale_block, scale_block, full + s);
               bulk_g2s(sc + scale_block, p.v_scale + static_cast<int64_t>(pid) * scale_block, scale_block, full + s);
@@ -755,21 +752,28 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 3-D view of k_data / v_data: (D/2 bytes, Hkv heads, NP*16 token rows); a
-// box is one head's 16 rows of one page.
-bool make_kv_map(CUtensorMap* map, const void* base, int D, int hkv, int64_t num_pages) {
+// 4-D view of k_data / v_data: (D/2 bytes, 16 tokens of a page, Hkv heads,
+// pages) with the token stride (Hkv*D/2) above the head stride (D/2).  A
+// box of (D/2, 16, hb, 1) lands as hb per-head [16][D/2] tiles, swizzled so
+// that ldmatrix reads them without bank conflicts: one copy per page per
+// tensor for the whole head block.
+bool make_kv_map(CUtensorMap* map, const void* base, int D, int hkv, int hb, int64_t num_pages) {
   EncodeTiledFn enc = encode_fn();
   if (enc == nullptr) return false;
-  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(D / 2), static_cast<cuuint64_t>(hkv),
-                              static_cast<cuuint64_t>(num_pages) * kPage};
-  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(D / 2), static_cast<cuuint64_t>(hkv) * (D / 2)};
-  const cuuint32_t box[3] = {static_cast<cuuint32_t>(D / 2), 1u, static_cast<cuuint32_t>(kPage)};
-  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(D / 2), static_cast<cuuint64_t>(kPage),
+                              static_cast<cuuint64_t>(hkv), static_cast<cuuint64_t>(num_pages)};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(hkv) * (D / 2), static_cast<cuuint64_t>(D / 2),
+                                 static_cast<cuuint64_t>(hkv) * (D / 2) * kPage};
+  const cuuint32_t box[4] = {static_cast<cuuint32_t>(D / 2), static_cast<cuuint32_t>(kPage),
+                             static_cast<cuuint32_t>(hb), 1u};
+  const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
   const CUtensorMapSwizzle sw = (D == 128) ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
-  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
+
+int pick_hb(int hkv);
 
 // KV heads per CTA: the largest power of two <= max_hb dividing Hkv.
 // IRIS_DECODE_MAX_HB (1, 2, 4 or 8) overrides the default of 4 for tuning.
@@ -1002,8 +1006,9 @@ extern "C" int iris_b200_int4_paged_decode(const void* query, const void* k_data
   if (workspace_bytes < ws.bytes) return IRIS_EWORKSPACE;
 
   CUtensorMap km, vm;
-  if (!make_kv_map(&km, k_data, head_dim, num_kv_heads, num_pages) ||
-      !make_kv_map(&vm, v_data, head_dim, num_kv_heads, num_pages)) {
+  const int hb = pick_hb(num_kv_heads);
+  if (!make_kv_map(&km, k_data, head_dim, num_kv_heads, hb, num_pages) ||
+      !make_kv_map(&vm, v_data, head_dim, num_kv_heads, hb, num_pages)) {
     snprintf(iris::g_last_error, sizeof(iris::g_last_error), "cuTensorMapEncodeTiled failed (D=%d Hkv=%d pages=%lld)", head_dim,
              num_kv_heads, static_cast<long long>(num_pages));
     return IRIS_ECUDA;
