@@ -146,6 +146,41 @@ IRIS_API int iris_b200_int4_paged_decode(const void* query, const void* k_data, 
                                 float softmax_scale, void* workspace, size_t workspace_bytes, int32_t* error_word,
                                 void* stream);
 
+/* Size of the scratch array iris_b200_int4_paged_decode_noalloc uses (32 MiB). */
+#define IRIS_DECODE_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/*
+ * iris_b200_int4_paged_decode for callers that cannot allocate device memory.
+ * No counterpart in the reference (its decode allocates nothing but its
+ * output; this library's split-KV decode needs a workspace).
+ *
+ * Same arguments and results as iris_b200_int4_paged_decode, without the
+ * workspace: the scratch (page prefix sums, split-KV partial records) is a
+ * static __device__ array of IRIS_DECODE_NOALLOC_SCRATCH_BYTES inside the
+ * library, held by every GPU that loads the library until the process exits.
+ * For callers that are handed their tensors and may not call cudaMalloc or an
+ * allocating library routine themselves (plugins in frameworks that own all
+ * device memory, code running in allocator or stream callbacks, serving loops
+ * that forbid allocation after start-up).
+ *   - Nothing is allocated; returns IRIS_EWORKSPACE, before touching the
+ *     array, when the problem needs more scratch than the array holds
+ *     (iris_b200_decode_workspace_bytes > IRIS_DECODE_NOALLOC_SCRATCH_BYTES).
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture.
+ *   - All calls share the one array: calls whose work overlaps on the GPU
+ *     (other streams, other host threads) race.  Each call rewrites the
+ *     parts it reads, so no state carries over between calls.
+ */
+IRIS_API int iris_b200_int4_paged_decode_noalloc(const void* query, const void* k_data, const void* v_data,
+                                                 const void* k_scale, const void* v_scale,
+                                                 const int32_t* block_table, int64_t block_table_stride,
+                                                 const int32_t* seq_lens, void* output, float* out_lse,
+                                                 int32_t out_mode, int32_t batch, int32_t num_q_heads,
+                                                 int32_t num_kv_heads, int32_t head_dim, int64_t num_pages,
+                                                 int32_t page_size, int32_t max_pages_per_seq, float softmax_scale,
+                                                 int32_t* error_word, void* stream);
+
 /*
  * Merge `num_parts` log-sum-exp-form partial results (as produced with
  * IRIS_DECODE_OUT_LSE) into the final fp16 output:

@@ -27,6 +27,8 @@ ERR_PIPELINE_TIMEOUT = 0x80
 DECODE_OUT_FP16 = 0
 DECODE_OUT_LSE = 1
 
+DECODE_NOALLOC_SCRATCH_BYTES = 32 << 20  # IRIS_DECODE_NOALLOC_SCRATCH_BYTES
+
 _c_i32, _c_i64, _c_sz, _c_p, _c_f = ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_float
 
 # name -> (restype, argtypes); must match include/iris_b200.h
@@ -45,6 +47,10 @@ SIGNATURES = {
         ctypes.c_int,
         [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
          _c_i64, _c_i32, _c_i32, _c_f, _c_p, _c_sz, _c_p, _c_p]),
+    "iris_b200_int4_paged_decode_noalloc": (
+        ctypes.c_int,
+        [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
+         _c_i64, _c_i32, _c_i32, _c_f, _c_p, _c_p]),
     "iris_b200_merge_lse_partials": (ctypes.c_int, [_c_p, _c_p, _c_i32, _c_i64, _c_i32, _c_p, _c_p]),
 }
 

@@ -1,0 +1,86 @@
+"""The allocation-free decode entry point, for callers that may not allocate
+device memory themselves (plugins handed their tensors by a framework that
+owns all device memory, code in allocator or stream callbacks, serving loops
+that forbid allocation after start-up): iris_b200_int4_paged_decode_noalloc
+keeps its scratch in a static array inside the library.
+
+Called through the C ABI twice in a row on different inputs (the second call
+reuses the scratch the first one left), each output must match the regular
+entry point's (which gets a workspace from the caller) within the decode
+tolerance of the other tests.  Collected last (file name) so that a run that
+stops at the first failure has run every other test first; it also passes
+alone in a fresh process."""
+import numpy as np
+import pytest
+import torch
+
+import cases
+from _refs import assert_decode_close, to_dev
+
+pytestmark = pytest.mark.gpu
+
+
+def _args(t, out, err):
+    q, kd, vd, ks, vs, bt, lens = (t[k] for k in cases.DECODE_KEYS)
+    B, Hq, D = q.shape
+    NP, P, Hkv, _ = kd.shape
+    head = [q.data_ptr(), kd.data_ptr(), vd.data_ptr(), ks.data_ptr(), vs.data_ptr(), bt.data_ptr(), bt.stride(0),
+            lens.data_ptr(), out.data_ptr(), None, 0, B, Hq, Hkv, D, NP, P, bt.shape[1], D ** -0.5]
+    return head, err.data_ptr(), torch.cuda.current_stream().cuda_stream
+
+
+def _regular(lib, t):
+    out = torch.empty_like(t["query"])
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    q = t["query"]
+    ws_bytes = lib.iris_b200_decode_workspace_bytes(q.shape[0], q.shape[1], t["k_data"].shape[2], q.shape[2], 0)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    head, errp, stream = _args(t, out, err)
+    assert lib.iris_b200_int4_paged_decode(*head, ws.data_ptr(), ws.numel(), errp, stream) == 0
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    return out
+
+
+def _noalloc(lib, t):
+    out = torch.empty_like(t["query"])
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    head, errp, stream = _args(t, out, err)
+    assert lib.iris_b200_int4_paged_decode_noalloc(*head, errp, stream) == 0
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    return out
+
+
+def test_noalloc_decode_matches_regular_entry_point_twice():
+    from iris_kernel import _lib
+
+    lib = _lib.lib
+    # long and short sequences, so split-KV records go through the scratch
+    first = cases.decode_random(seed=71, B=4, Hq=16, Hkv=4, D=128, lens=[3000, 17, 900, 5000])
+    second = cases.decode_random(seed=72, B=3, Hq=8, Hkv=8, D=64, lens=[2500, 40, 1234])
+    for c in (first, second):
+        t = to_dev(c, cases.DECODE_KEYS)
+        got = _noalloc(lib, t)
+        ref = _regular(lib, t)
+        assert_decode_close(got, ref)
+    # and once more on the first input after the second call changed the scratch
+    t = to_dev(first, cases.DECODE_KEYS)
+    assert_decode_close(_noalloc(lib, t), _regular(lib, t))
+
+
+def test_noalloc_rejects_problems_larger_than_its_scratch():
+    from iris_kernel import _lib
+
+    lib = _lib.lib
+    # MQA with 16 query heads at D=128 needs more split-KV records than the array holds
+    need = lib.iris_b200_decode_workspace_bytes(1, 16, 1, 128, 0)
+    assert need > _lib.DECODE_NOALLOC_SCRATCH_BYTES
+    c = cases.decode_random(seed=73, B=1, Hq=16, Hkv=1, D=128, lens=[64])
+    t = to_dev(c, cases.DECODE_KEYS)
+    out = torch.full_like(t["query"], float("nan"))
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    head, errp, stream = _args(t, out, err)
+    assert lib.iris_b200_int4_paged_decode_noalloc(*head, errp, stream) == 5  # IRIS_EWORKSPACE
+    torch.cuda.synchronize()
+    assert bool(torch.isnan(out).all())  # nothing was launched
