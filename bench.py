@@ -52,6 +52,11 @@ APPEND_BYTES = B * HKV * (4 * D + D + D // 8) + B * 8 + 2 * (D // 2) * 2
 STEP_BYTES = DECODE_BYTES + APPEND_BYTES
 SPEC_TBS = 8.0
 
+# BASELINE config 5b: prefill-style append, 8 sequences x 8192 new tokens,
+# Hkv=8, D=128, fresh permuted pages, 1% of entries x20, RoPE base 500000.
+PF_S, PF_L = 8, 8192
+PF_BYTES = PF_S * PF_L * HKV * (4 * D + D + D // 8) + PF_S * PF_L * 8 + PF_L * 2 * (D // 2) * 2
+
 
 def _peak_gbs():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -166,6 +171,35 @@ def build_workload(dev, seed):
                                                                              device=dev))
     torch.cuda.synchronize(dev)
     return w
+
+
+def build_prefill(dev, seed):
+    from oracle import iris_oracle as orc  # RoPE table builder only (host arrays)
+
+    g = torch.Generator(device=dev).manual_seed(seed)
+    T = PF_S * PF_L
+    k = torch.randn(T, HKV, D, generator=g, device=dev)
+    v = torch.randn(T, HKV, D, generator=g, device=dev)
+    k[torch.rand(k.shape, generator=g, device=dev) < 0.01] *= 20
+    v[torch.rand(v.shape, generator=g, device=dev) < 0.01] *= 20
+    npages = T // P
+    pages = torch.randperm(npages, generator=g, device=dev).view(PF_S, PF_L // P)
+    pos = torch.arange(PF_L, device=dev, dtype=torch.int32).repeat(PF_S)
+    slots = (pages.repeat_interleave(P, dim=1) * P + torch.arange(PF_L, device=dev) % P).view(-1).int()
+    cos_np, sin_np = orc.rope_cache(PF_L, D, 500000.0)
+    return dict(k=k.half(), v=v.half(), pos=pos, slots=slots.contiguous(), cos=torch.from_numpy(cos_np).to(dev),
+                sin=torch.from_numpy(sin_np).to(dev),
+                kd=torch.zeros(npages, P, HKV, D // 2, dtype=torch.uint8, device=dev),
+                vd=torch.zeros(npages, P, HKV, D // 2, dtype=torch.uint8, device=dev),
+                ks=torch.zeros(npages, P, HKV, D // G, dtype=torch.float16, device=dev),
+                vs=torch.zeros(npages, P, HKV, D // G, dtype=torch.float16, device=dev))
+
+
+def step_prefill(x):
+    from iris_kernel.fused_kv import fused_rope_int4_paged_append
+
+    fused_rope_int4_paged_append(x["k"], x["v"], x["pos"], x["slots"], x["cos"], x["sin"], x["kd"], x["vd"], x["ks"],
+                                 x["vs"], rotary_dim=D, page_size=P)
 
 
 def step_decode(w):
@@ -334,6 +368,17 @@ def main():
     ms_app = timed(g_app.replay, args.steps, dev, dist, args.warmup)
     iris_kernel.check_errors(dev)
     iris_kernel.set_validation_mode("sync")
+    # config 5b prefill append (its own inputs; not part of the step)
+    x = build_prefill(dev, seed=99 + rank)
+    iris_kernel.set_validation_mode("deferred")
+    g_pf = graph_of(lambda: step_prefill(x), dev)
+    pf_steps = max(10, min(args.steps, 200))
+    ms_pf = timed(g_pf.replay, pf_steps, dev, dist, args.warmup)
+    iris_kernel.check_errors(dev)
+    iris_kernel.set_validation_mode("sync")
+    del g_pf, x
+    ms_pf = max_over_ranks(ms_pf, dist, dev)
+    pf_us = ms_pf / pf_steps * 1e3
     ms = max_over_ranks(ms, dist, dev)
     ms_dec = max_over_ranks(ms_dec, dist, dev)
     ms_app = max_over_ranks(ms_app, dist, dev)
@@ -401,6 +446,10 @@ def main():
             "decode_pct_of_8tbs": 100 * DECODE_BYTES / (dec_us * 1e-6) / 1e12 / SPEC_TBS,
             "decode_pct_of_measured": 100 * achieved / peak,
             "append_us": app_us, "append_tokens_per_s": world * B / (app_us * 1e-6),
+            "prefill_append": {"config": "BASELINE config 5b: 8 x 8192 tokens, Hkv 8, D 128",
+                               "us": pf_us, "tbs": world * PF_BYTES / (pf_us * 1e-6) / 1e12,
+                               "pct_of_measured": 100 * PF_BYTES / (pf_us * 1e-6) / 1e9 / _peak_gbs()[0],
+                               "tokens_per_s": world * PF_S * PF_L / (pf_us * 1e-6), "bytes": PF_BYTES},
             "step_bytes": STEP_BYTES, "decode_bytes": DECODE_BYTES, "append_bytes": APPEND_BYTES,
             "e2e": {"value": e2e_value, "unit": "TB/s", "ms_per_step": ms_e2e / args.steps,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},

@@ -63,7 +63,9 @@ IRIS_DEV __half group_scale(__half amax) {
   return __float2half_rn(s);
 }
 
-IRIS_DEV uint32_t quant_pack8(const __half2 (&v)[4], float scale) {
+// Reference semantics, IEEE division: q = clamp(rint(x / scale), -7, 7).
+// Used for non-finite scales (a group holding Inf or NaN).
+IRIS_DEV uint32_t quant_pack8_ieee(const __half2 (&v)[4], float scale) {
   uint32_t word = 0;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -74,6 +76,48 @@ IRIS_DEV uint32_t quant_pack8(const __half2 (&v)[4], float scale) {
     q1 = min(7, max(-7, q1));
     word |= (static_cast<uint32_t>(q0) & 0xFu) << (8 * i);
     word |= (static_cast<uint32_t>(q1) & 0xFu) << (8 * i + 4);
+  }
+  return word;
+}
+
+IRIS_DEV float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// The same result without a division, for a finite group scale.
+//
+// x and scale are fp16 values, so x / scale = X 2^a / (S 2^b) with 11-bit
+// integers X, S.  If the quotient is not exactly a half-integer it is at
+// least 2^-13 away from one (for |q| >= 1/4 the numerator x - (k+1/2) scale
+// is a non-zero multiple of 2^(e_scale - 12) and scale < 2^(e_scale + 1)),
+// while the fp32 quotient is off by at most 7.5 * 2^-24: IEEE rounding and
+// round-half-even then agree with any estimate that close.  y = x * rcp(scale) is within ~2^-21 relative;
+// one Markstein residual step (Markstein 1990: e = x - y*scale, exact in one
+// FMA since it has at most 13 significant bits; y += e * rcp) lands within
+// |q| 2^-43 of q before rounding, so exact half-integers come out exact, so the ties
+// also round to even.  Adding 2^23 + 16 rounds y to the nearest integer,
+// ties to even, and leaves (q + 16) mod 16 -- the two's-complement nibble --
+// in the low four mantissa bits.  |x| <= amax and scale = fp16(amax / 7)
+// (or 2^-14) keep |q| <= 7, so the reference's clamp never binds here.
+// Checked against the IEEE path on every exact tie and a dense sweep
+// (tests/test_gpu_append.py).
+IRIS_DEV uint32_t quant_pack8(const __half2 (&v)[4], float scale) {
+  if (!(fabsf(scale) <= 3.0e38f)) return quant_pack8_ieee(v, scale);
+  const float r = rcp_approx(scale);
+  const float kRound = 8388624.0f;  // 2^23 + 16
+  uint32_t word = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(v[i]);
+    float y0 = __fmul_rn(f.x, r);
+    float y1 = __fmul_rn(f.y, r);
+    y0 = fmaf(fmaf(-y0, scale, f.x), r, y0);
+    y1 = fmaf(fmaf(-y1, scale, f.y), r, y1);
+    const uint32_t n0 = __float_as_uint(__fadd_rn(y0, kRound)) & 0xFu;
+    const uint32_t n1 = __float_as_uint(__fadd_rn(y1, kRound)) & 0xFu;
+    word |= (n0 | (n1 << 4)) << (8 * i);
   }
   return word;
 }

@@ -245,3 +245,63 @@ def test_unsupported_shapes_raise():
     with pytest.raises(TypeError):
         fused_rope_int4_paged_append(t["key"], t["value"], t["positions"].long(), t["slot_mapping"], t["cos_cache"],
                                      t["sin_cache"], *[t[k] for k in CACHE], rotary_dim=128, page_size=16)
+
+
+def _quant_case(groups):
+    """Wrap [N, 32] fp16 groups as a V-only append (identity RoPE on K too)."""
+    n = groups.shape[0]
+    pad = (-n) % 64
+    if pad:
+        groups = np.concatenate([groups, np.zeros((pad, 32), np.float16)])
+    T = groups.shape[0] // 4
+    val = groups.reshape(T, 1, 128)
+    NPg = T // 16
+    return dict(key=val[::-1].copy(), value=val, positions=np.zeros(T, np.int32),
+                slot_mapping=np.arange(T, dtype=np.int32), cos_cache=np.ones((1, 64), np.float16),
+                sin_cache=np.zeros((1, 64), np.float16), k_data=np.zeros((NPg, 16, 1, 64), np.uint8),
+                v_data=np.zeros((NPg, 16, 1, 64), np.uint8), k_scale=np.zeros((NPg, 16, 1, 4), np.float16),
+                v_scale=np.zeros((NPg, 16, 1, 4), np.float16), rotary_dim=128, group_size=32, page_size=16)
+
+
+def test_quantiser_every_exact_tie():
+    """Every (amax, k) with x = (k + 1/2) * scale representable in fp16 and
+    |x| <= amax: the quotient is exactly a half-integer and must round to
+    even, as the reference's IEEE division + torch.round do."""
+    amax = np.arange(1, 0x7C00, dtype=np.uint16).view(np.float16)
+    a32 = amax.astype(np.float32)
+    s = np.maximum(a32 / np.float32(7.0), np.float32(2.0 ** -14)).astype(np.float16).astype(np.float32)
+    rows = []
+    for k in range(-8, 8):
+        x = ((k + 0.5) * s).astype(np.float32)
+        ok = (x.astype(np.float16).astype(np.float32) == x) & (np.abs(x) <= a32)
+        rows.append(np.stack([a32[ok], x[ok]], 1))
+    pairs = np.concatenate(rows)
+    assert len(pairs) > 50000
+    g = np.zeros((len(pairs), 32), np.float32)
+    g[:, 0] = pairs[:, 0]
+    g[:, 1:] = pairs[:, 1:2]  # the tie value in 31 slots
+    g[:, 2] = -pairs[:, 1]
+    c = _quant_case(g.astype(np.float16))
+    _assert_bytes_equal(_fused(c), _oracle(c))
+
+
+def test_quantiser_dense_sweep():
+    """For 600 amax values spread over the fp16 range, every fp16 x with
+    |x| <= amax (both signs), against the oracle's IEEE division."""
+    rng = np.random.default_rng(2024)
+    pick = np.unique(np.concatenate([rng.integers(1, 0x7C00, 560), np.arange(0x3C00 - 20, 0x3C00 + 20)]))
+    allx = np.arange(0, 0x7C00, dtype=np.uint16).view(np.float16).astype(np.float32)
+    groups = []
+    for bits in pick:
+        a = np.array([bits], np.uint16).view(np.float16).astype(np.float32)[0]
+        xs = allx[allx <= a]
+        xs = np.concatenate([xs, -xs])
+        n = (len(xs) + 30) // 31
+        body = np.zeros(n * 31, np.float32)
+        body[:len(xs)] = xs
+        grp = np.concatenate([np.full((n, 1), a, np.float32), body.reshape(n, 31)], 1)
+        groups.append(grp)
+    g = np.concatenate(groups).astype(np.float16)
+    assert g.shape[0] > 100000
+    c = _quant_case(g)
+    _assert_bytes_equal(_fused(c), _oracle(c))
