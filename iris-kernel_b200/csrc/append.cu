@@ -21,6 +21,23 @@
 
 namespace iris {
 
+// Division of non-negative 32-bit integers n < 2^31 by a divisor fixed at
+// launch: q = (umulhi(n, m) + n) >> l with l = ceil(log2 d) and
+// m = floor(2^32 (2^l - d) / d) + 1 (Granlund & Montgomery, "Division by
+// Invariant Integers using Multiplication", 1994).
+struct FastDiv {
+  uint32_t d, m, l;
+  static FastDiv make(uint32_t d) {
+    FastDiv f;
+    f.d = d;
+    f.l = 0;
+    while ((1ull << f.l) < d) ++f.l;
+    f.m = static_cast<uint32_t>(((1ull << 32) * ((1ull << f.l) - d)) / d + 1);
+    return f;
+  }
+  IRIS_DEV uint32_t div(uint32_t n) const { return (__umulhi(n, m) + n) >> l; }
+};
+
 struct AppendParams {
   const __half* key;
   const __half* value;
@@ -37,6 +54,8 @@ struct AppendParams {
   int64_t num_slots;  // num_pages * page_size
   int32_t num_heads;
   int32_t page_size;
+  FastDiv heads_div;  // row -> (token, head)
+  FastDiv page_div;   // slot -> (page, offset)
   int32_t* err;
 };
 
@@ -56,8 +75,23 @@ IRIS_DEV __half habs_max8(const __half2 (&v)[4]) {
 }
 
 // fp16 group scale from the group's absmax, exactly as the eager reference.
+//
+// amax / 7 is rounded with one Markstein residual step instead of a division:
+// amax = A 2^e with an 11-bit A, so amax / 7 either is exact (7 | A) or has a
+// non-terminating period-3 binary expansion that stays at least ~2^-28
+// (relative) away from every fp32 rounding midpoint, while the corrected
+// estimate is within 2^-43 before its final rounding: both round alike.
+// Checked against the IEEE division for all 31,744 finite fp16 values.
 IRIS_DEV __half group_scale(__half amax) {
-  float s = __fdiv_rn(__half2float(amax), 7.0f);
+  const float a = __half2float(amax);
+  float s;
+  if (a <= 65504.0f) {
+    const float r7 = 0.142857149f;  // fp32(1/7)
+    const float y = __fmul_rn(a, r7);
+    s = fmaf(fmaf(-y, 7.0f, a), r7, y);
+  } else {
+    s = __fdiv_rn(a, 7.0f);  // Inf / NaN
+  }
   const float tiny = 6.103515625e-05f;  // 2^-14 = torch.finfo(float16).tiny
   s = (s < tiny) ? tiny : s;            // NaN stays NaN (torch clamp_min)
   return __float2half_rn(s);
@@ -156,8 +190,9 @@ __global__ void __launch_bounds__(AppendCfg<D>::kThreads) rope_int4_append_kerne
   const int64_t row = static_cast<int64_t>(blockIdx.x) * C::kRows + tid / C::kTpr;
   const int64_t nrows = p.num_tokens * p.num_heads;
   const bool in_range = row < nrows;
-  const int64_t tok = in_range ? row / p.num_heads : 0;
-  const int h = in_range ? static_cast<int>(row % p.num_heads) : 0;
+  const uint32_t tok32 = in_range ? p.heads_div.div(static_cast<uint32_t>(row)) : 0u;
+  const int64_t tok = tok32;
+  const int h = in_range ? static_cast<int>(static_cast<uint32_t>(row) - tok32 * static_cast<uint32_t>(p.num_heads)) : 0;
 
   int32_t slot = in_range ? __ldg(p.slots + tok) : -1;
   int32_t pos = 0;
@@ -223,8 +258,9 @@ __global__ void __launch_bounds__(AppendCfg<D>::kThreads) rope_int4_append_kerne
   const uint32_t vword = quant_pack8(vv, __half2float(vs));
 
   // ---- stores ----
-  const int64_t page = active ? slot / p.page_size : 0;
-  const int64_t off = active ? slot % p.page_size : 0;
+  const uint32_t page32 = active ? p.page_div.div(static_cast<uint32_t>(slot)) : 0u;
+  const int64_t page = page32;
+  const int64_t off = active ? static_cast<uint32_t>(slot) - page32 * static_cast<uint32_t>(p.page_size) : 0;
   const int64_t crow = (page * p.page_size + off) * p.num_heads + h;  // cache row
   if (active) {
     reinterpret_cast<uint32_t*>(p.k_data + crow * (D / 2))[c] = kword;
@@ -362,6 +398,7 @@ extern "C" int iris_b200_rope_int4_paged_append(const void* key, const void* val
     return IRIS_EINVAL;
   if (head_dim <= 0 || head_dim % 64 != 0 || head_dim > 512) return IRIS_EUNSUPPORTED;
   if (num_tokens == 0) return IRIS_OK;
+  if (num_tokens * num_kv_heads >= (1ll << 31) || num_pages * page_size >= (1ll << 31)) return IRIS_EUNSUPPORTED;
   const void* ptrs[] = {key, value, positions, slot_mapping, cos_cache, sin_cache, k_data, v_data, k_scale, v_scale};
   for (const void* q : ptrs)
     if (q == nullptr) return IRIS_EINVAL;
@@ -384,6 +421,8 @@ extern "C" int iris_b200_rope_int4_paged_append(const void* key, const void* val
   p.num_slots = num_pages * page_size;
   p.num_heads = num_kv_heads;
   p.page_size = page_size;
+  p.heads_div = FastDiv::make(static_cast<uint32_t>(num_kv_heads));
+  p.page_div = FastDiv::make(static_cast<uint32_t>(page_size));
   p.err = error_word;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   clear_stale_cuda_error();
