@@ -10,13 +10,11 @@
 // round-half-to-even (:83-86), byte = q[2i] & 0xF | (q[2i+1] & 0xF) << 4
 // (:104-107).
 //
-// Layout of the work: one thread owns 8 consecutive dims (one 16-byte fp16
-// vector) of one (token, kv-head) row, for both K and V.  A row is D/8
-// threads; a 32-dim quantisation group is 4 adjacent lanes, reduced with two
-// xor-shuffles.  Loads are 128-bit and coalesced, packed stores are 32-bit
-// per thread (64 contiguous bytes per row for D=128) and the row's scales
-// leave in one vector store.  The kernel is HBM-bound: per (token, head) it
-// moves 4D bytes in and D + D/8 bytes out.
+// Layout of the work: one thread owns one 32-dim quantisation group of one
+// (token, kv-head) row, for both K and V (D/32 threads per row), so the group
+// absmax and scale need no communication and the 16 packed bytes leave in
+// one vector store.  The kernel is HBM-bound: per (token, head) it moves 4D
+// bytes in and D + D/8 bytes out.
 #include "common.cuh"
 
 namespace iris {
@@ -67,12 +65,6 @@ IRIS_DEV uint4 ldg_nc_v4(const void* p) {
   return r;
 }
 
-IRIS_DEV __half habs_max8(const __half2 (&v)[4]) {
-  // NaN-propagating, like torch's amax.
-  __half2 m = __hmax2_nan(__habs2(v[0]), __habs2(v[1]));
-  m = __hmax2_nan(m, __hmax2_nan(__habs2(v[2]), __habs2(v[3])));
-  return __hmax_nan(__low2half(m), __high2half(m));
-}
 
 // fp16 group scale from the group's absmax, exactly as the eager reference.
 //
@@ -120,6 +112,7 @@ IRIS_DEV float rcp_approx(float x) {
   return y;
 }
 
+
 // The same result without a division, for a finite group scale.
 //
 // x and scale are fp16 values, so x / scale = X 2^a / (S 2^b) with 11-bit
@@ -137,9 +130,15 @@ IRIS_DEV float rcp_approx(float x) {
 // (or 2^-14) keep |q| <= 7, so the reference's clamp never binds here.
 // Checked against the IEEE path on every exact tie and a dense sweep
 // (tests/test_gpu_append.py).
-IRIS_DEV uint32_t quant_pack8(const __half2 (&v)[4], float scale) {
-  if (!(fabsf(scale) <= 3.0e38f)) return quant_pack8_ieee(v, scale);
-  const float r = rcp_approx(scale);
+//
+// 8 fp16 values (one 16-byte vector) -> 8 nibbles (one 32-bit word); `fast`
+// is false for a non-finite scale (IEEE path).
+IRIS_DEV uint32_t quant_pack_vec(const uint4& raw, float scale, float r, bool fast) {
+  const __half2* v = reinterpret_cast<const __half2*>(&raw);
+  if (!fast) {
+    const __half2 vv[4] = {v[0], v[1], v[2], v[3]};
+    return quant_pack8_ieee(vv, scale);
+  }
   const float kRound = 8388624.0f;  // 2^23 + 16
   uint32_t word = 0;
 #pragma unroll
@@ -156,160 +155,112 @@ IRIS_DEV uint32_t quant_pack8(const __half2 (&v)[4], float scale) {
   return word;
 }
 
-IRIS_DEV __half shfl_half(__half v, int src, uint32_t mask) {
-  unsigned short u = __half_as_ushort(v);
-  u = static_cast<unsigned short>(__shfl_sync(mask, static_cast<unsigned>(u), src));
-  return __ushort_as_half(u);
+IRIS_DEV __half2 habs_max_vec(const uint4& raw) {
+  const __half2* v = reinterpret_cast<const __half2*>(&raw);
+  return __hmax2_nan(__hmax2_nan(__habs2(v[0]), __habs2(v[1])), __hmax2_nan(__habs2(v[2]), __habs2(v[3])));
 }
 
-IRIS_DEV __half shfl_xor_half(__half v, int x) {
-  unsigned short u = __half_as_ushort(v);
-  u = static_cast<unsigned short>(__shfl_xor_sync(0xffffffffu, static_cast<unsigned>(u), x));
-  return __ushort_as_half(u);
+// One 32-dim quantisation group (4 vectors): fp16 scale and 4 packed words.
+IRIS_DEV void quant_group(const uint4 (&g)[4], __half& scale16, uint4& packed) {
+  __half2 m = __hmax2_nan(__hmax2_nan(habs_max_vec(g[0]), habs_max_vec(g[1])),
+                          __hmax2_nan(habs_max_vec(g[2]), habs_max_vec(g[3])));
+  scale16 = group_scale(__hmax_nan(__low2half(m), __high2half(m)));
+  const float sc = __half2float(scale16);
+  const bool fast = fabsf(sc) <= 3.0e38f;  // finite: division-free path
+  const float r = rcp_approx(sc);
+  packed.x = quant_pack_vec(g[0], sc, r, fast);
+  packed.y = quant_pack_vec(g[1], sc, r, fast);
+  packed.z = quant_pack_vec(g[2], sc, r, fast);
+  packed.w = quant_pack_vec(g[3], sc, r, fast);
 }
 
+// One thread owns one 32-dim quantisation group of one (token, kv-head) row,
+// for both K and V: D/32 threads per row.  The group's absmax and scale are
+// thread-local, its 16 packed bytes leave in one vector store.  The RoPE
+// partner group (dims +-D/2) is read again by this thread (an L1 hit: the
+// partner thread loads it too).
 template <int D>
 struct AppendCfg {
-  static constexpr int kTpr = D / 8;                            // threads per (token, head) row
-  // rows per CTA: as many as fit in 256 threads while keeping whole warps
-  static constexpr int kRowQuant = 32 / (kTpr % 32 == 0 ? 32 : (kTpr % 16 == 0 ? 16 : 8));
-  static constexpr int kRows = (256 / kTpr) / kRowQuant * kRowQuant;
+  static constexpr int kTpr = D / 32;                    // threads per row
+  static constexpr int kHalf = kTpr / 2;                 // partner distance in groups
+  static constexpr int kRows = 128 / kTpr;               // rows per CTA
   static constexpr int kThreads = kRows * kTpr;
-  static constexpr int kHalf = kTpr / 2;                        // RoPE partner distance in chunks
-  // partner via shuffle when a row sits inside one warp at a power-of-two width
-  static constexpr bool kShuffle = kTpr <= 32 && (32 % kTpr) == 0;
-  static constexpr int kGroups = D / 32;
-  static constexpr bool kVecScale = kShuffle && (kGroups == 2 || kGroups == 4 || kGroups == 8);
 };
 
 template <int D>
 __global__ void __launch_bounds__(AppendCfg<D>::kThreads) rope_int4_append_kernel(const AppendParams p) {
   using C = AppendCfg<D>;
   const int tid = threadIdx.x;
-  const int c = tid % C::kTpr;  // chunk of 8 dims within the row
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * C::kRows + tid / C::kTpr;
-  const int64_t nrows = p.num_tokens * p.num_heads;
-  const bool in_range = row < nrows;
-  const uint32_t tok32 = in_range ? p.heads_div.div(static_cast<uint32_t>(row)) : 0u;
-  const int64_t tok = tok32;
-  const int h = in_range ? static_cast<int>(static_cast<uint32_t>(row) - tok32 * static_cast<uint32_t>(p.num_heads)) : 0;
+  const int c = tid % C::kTpr;  // group within the row
+  const uint32_t row = blockIdx.x * C::kRows + tid / C::kTpr;
+  const uint32_t nrows = static_cast<uint32_t>(p.num_tokens) * static_cast<uint32_t>(p.num_heads);
+  if (row >= nrows) return;  // no collective operations below
+  const uint32_t tok = p.heads_div.div(row);
+  const uint32_t h = row - tok * static_cast<uint32_t>(p.num_heads);
 
-  int32_t slot = in_range ? __ldg(p.slots + tok) : -1;
-  int32_t pos = 0;
-  bool active = slot >= 0;
-  if (active) {
-    pos = __ldg(p.positions + tok);
+  const int32_t slot = __ldg(p.slots + tok);
+  if (slot < 0) return;
+  const int32_t pos = __ldg(p.positions + tok);
+  {
     int32_t bits = 0;
     if (static_cast<int64_t>(slot) >= p.num_slots) bits |= IRIS_ERR_SLOT_RANGE;
     if (pos < 0) bits |= IRIS_ERR_POS_NEGATIVE;
     else if (static_cast<int64_t>(pos) >= p.max_position) bits |= IRIS_ERR_POS_RANGE;
-    if (bits) {
+    if (bits) {  // never touch memory outside the cache / RoPE tables
       if (h == 0 && c == 0) set_error(p.err, bits);
-      active = false;  // never touch memory outside the cache / RoPE tables
+      return;
     }
   }
 
-  // ---- loads (inactive rows read nothing and compute on zeros) ----
+  // ---- loads ----
   const bool lo_half = c < C::kHalf;
-  const int pair = lo_half ? c : c - C::kHalf;  // chunk index into cos/sin
-  uint4 kr = make_uint4(0, 0, 0, 0), vr = kr, cr = kr, sr = kr, kp = kr;
-  const int64_t rowoff = (tok * p.num_heads + h) * static_cast<int64_t>(D);
-  if (active) {
-    kr = ldg_nc_v4(p.key + rowoff + 8 * c);
-    vr = ldg_nc_v4(p.value + rowoff + 8 * c);
-    cr = ldg_nc_v4(p.cos_cache + static_cast<int64_t>(pos) * (D / 2) + 8 * pair);
-    sr = ldg_nc_v4(p.sin_cache + static_cast<int64_t>(pos) * (D / 2) + 8 * pair);
-    if constexpr (!C::kShuffle) {
-      kp = ldg_nc_v4(p.key + rowoff + 8 * (lo_half ? c + C::kHalf : c - C::kHalf));
-    }
-  }
-  if constexpr (C::kShuffle) {
-    kp.x = __shfl_xor_sync(0xffffffffu, kr.x, C::kHalf);
-    kp.y = __shfl_xor_sync(0xffffffffu, kr.y, C::kHalf);
-    kp.z = __shfl_xor_sync(0xffffffffu, kr.z, C::kHalf);
-    kp.w = __shfl_xor_sync(0xffffffffu, kr.w, C::kHalf);
+  const int pair = lo_half ? c : c - C::kHalf;  // group index into cos/sin
+  const int partner = lo_half ? c + C::kHalf : c - C::kHalf;
+  const __half* krow = p.key + static_cast<size_t>(row) * D;
+  const __half* vrow = p.value + static_cast<size_t>(row) * D;
+  const __half* crow = p.cos_cache + static_cast<size_t>(pos) * (D / 2) + 32 * pair;
+  const __half* srow = p.sin_cache + static_cast<size_t>(pos) * (D / 2) + 32 * pair;
+  uint4 ko[4], kp[4], vo[4], cs[4], sn[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    ko[i] = ldg_nc_v4(krow + 32 * c + 8 * i);
+    kp[i] = ldg_nc_v4(krow + 32 * partner + 8 * i);
+    vo[i] = ldg_nc_v4(vrow + 32 * c + 8 * i);
+    cs[i] = ldg_nc_v4(crow + 8 * i);
+    sn[i] = ldg_nc_v4(srow + 8 * i);
   }
 
   // ---- RoPE, fp16 rounding after each op ----
   // low half:  y = x1*cos - x2*sin   (own = x1, partner = x2)
   // high half: y = x2*cos + x1*sin   (own = x2, partner = x1)
   // written as own*cos + (+-partner)*sin; negation is exact.
-  const __half2* kown = reinterpret_cast<const __half2*>(&kr);
-  const __half2* kpar = reinterpret_cast<const __half2*>(&kp);
-  const __half2* cs = reinterpret_cast<const __half2*>(&cr);
-  const __half2* sn = reinterpret_cast<const __half2*>(&sr);
-  __half2 kv[4], vv[4];
+  uint4 kr[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const __half2 par = lo_half ? __hneg2(kpar[i]) : kpar[i];
-    kv[i] = __hadd2(__hmul2_rn(kown[i], cs[i]), __hmul2_rn(par, sn[i]));
-    vv[i] = reinterpret_cast<const __half2*>(&vr)[i];
-  }
-
-  // ---- group absmax over 4 lanes, fp16 scales ----
-  __half kmax = habs_max8(kv), vmax = habs_max8(vv);
-  kmax = __hmax_nan(kmax, shfl_xor_half(kmax, 1));
-  vmax = __hmax_nan(vmax, shfl_xor_half(vmax, 1));
-  kmax = __hmax_nan(kmax, shfl_xor_half(kmax, 2));
-  vmax = __hmax_nan(vmax, shfl_xor_half(vmax, 2));
-  const __half ks = group_scale(kmax), vs = group_scale(vmax);
-
-  const uint32_t kword = quant_pack8(kv, __half2float(ks));
-  const uint32_t vword = quant_pack8(vv, __half2float(vs));
-
-  // ---- stores ----
-  const uint32_t page32 = active ? p.page_div.div(static_cast<uint32_t>(slot)) : 0u;
-  const int64_t page = page32;
-  const int64_t off = active ? static_cast<uint32_t>(slot) - page32 * static_cast<uint32_t>(p.page_size) : 0;
-  const int64_t crow = (page * p.page_size + off) * p.num_heads + h;  // cache row
-  if (active) {
-    reinterpret_cast<uint32_t*>(p.k_data + crow * (D / 2))[c] = kword;
-    reinterpret_cast<uint32_t*>(p.v_data + crow * (D / 2))[c] = vword;
-  }
-  if constexpr (C::kVecScale) {
-    // gather the row's group scales into lane c == 0 and store them at once
-    const int lane = tid & 31;
-    const int base = lane - c;
-    __half kg[C::kGroups], vg[C::kGroups];
+    const __half2* own = reinterpret_cast<const __half2*>(&ko[i]);
+    const __half2* par = reinterpret_cast<const __half2*>(&kp[i]);
+    const __half2* cc = reinterpret_cast<const __half2*>(&cs[i]);
+    const __half2* ss = reinterpret_cast<const __half2*>(&sn[i]);
+    __half2* out = reinterpret_cast<__half2*>(&kr[i]);
 #pragma unroll
-    for (int g = 0; g < C::kGroups; ++g) {
-      kg[g] = shfl_half(ks, base + 4 * g, 0xffffffffu);
-      vg[g] = shfl_half(vs, base + 4 * g, 0xffffffffu);
-    }
-    if (active && c == 0) {
-      __half* kdst = p.k_scale + crow * C::kGroups;
-      __half* vdst = p.v_scale + crow * C::kGroups;
-      if constexpr (C::kGroups == 2) {
-        *reinterpret_cast<__half2*>(kdst) = __halves2half2(kg[0], kg[1]);
-        *reinterpret_cast<__half2*>(vdst) = __halves2half2(vg[0], vg[1]);
-      } else if constexpr (C::kGroups == 4) {
-        uint2 kk, vvv;
-        kk.x = h2_as_u32(__halves2half2(kg[0], kg[1]));
-        kk.y = h2_as_u32(__halves2half2(kg[2], kg[3]));
-        vvv.x = h2_as_u32(__halves2half2(vg[0], vg[1]));
-        vvv.y = h2_as_u32(__halves2half2(vg[2], vg[3]));
-        *reinterpret_cast<uint2*>(kdst) = kk;
-        *reinterpret_cast<uint2*>(vdst) = vvv;
-      } else {
-        uint4 kk, vvv;
-        kk.x = h2_as_u32(__halves2half2(kg[0], kg[1]));
-        kk.y = h2_as_u32(__halves2half2(kg[2], kg[3]));
-        kk.z = h2_as_u32(__halves2half2(kg[4], kg[5]));
-        kk.w = h2_as_u32(__halves2half2(kg[6], kg[7]));
-        vvv.x = h2_as_u32(__halves2half2(vg[0], vg[1]));
-        vvv.y = h2_as_u32(__halves2half2(vg[2], vg[3]));
-        vvv.z = h2_as_u32(__halves2half2(vg[4], vg[5]));
-        vvv.w = h2_as_u32(__halves2half2(vg[6], vg[7]));
-        *reinterpret_cast<uint4*>(kdst) = kk;
-        *reinterpret_cast<uint4*>(vdst) = vvv;
-      }
-    }
-  } else {
-    if (active && (c & 3) == 0) {
-      p.k_scale[crow * C::kGroups + c / 4] = ks;
-      p.v_scale[crow * C::kGroups + c / 4] = vs;
+    for (int j = 0; j < 4; ++j) {
+      const __half2 pj = lo_half ? __hneg2(par[j]) : par[j];
+      out[j] = __hadd2(__hmul2_rn(own[j], cc[j]), __hmul2_rn(pj, ss[j]));
     }
   }
+
+  // ---- quantise, pack, store ----
+  __half ks, vs;
+  uint4 kw, vw;
+  quant_group(kr, ks, kw);
+  quant_group(vo, vs, vw);
+  const uint32_t page = p.page_div.div(static_cast<uint32_t>(slot));
+  const uint32_t off = static_cast<uint32_t>(slot) - page * static_cast<uint32_t>(p.page_size);
+  const size_t crow_idx = (static_cast<size_t>(page) * p.page_size + off) * p.num_heads + h;  // cache row
+  *reinterpret_cast<uint4*>(p.k_data + crow_idx * (D / 2) + 16 * c) = kw;
+  *reinterpret_cast<uint4*>(p.v_data + crow_idx * (D / 2) + 16 * c) = vw;
+  p.k_scale[crow_idx * (D / 32) + c] = ks;
+  p.v_scale[crow_idx * (D / 32) + c] = vs;
 }
 
 // One thread per token: range checks and duplicate detection through a
@@ -403,7 +354,7 @@ extern "C" int iris_b200_rope_int4_paged_append(const void* key, const void* val
   for (const void* q : ptrs)
     if (q == nullptr) return IRIS_EINVAL;
   if (!aligned(key, 16) || !aligned(value, 16) || !aligned(cos_cache, 16) || !aligned(sin_cache, 16) ||
-      !aligned(k_data, 4) || !aligned(v_data, 4) || !aligned(k_scale, 16) || !aligned(v_scale, 16))
+      !aligned(k_data, 16) || !aligned(v_data, 16) || !aligned(k_scale, 2) || !aligned(v_scale, 2))
     return IRIS_EALIGN;
   AppendParams p;
   p.key = static_cast<const __half*>(key);
