@@ -186,11 +186,23 @@ IRIS_API int iris_b200_int4_paged_decode_noalloc(const void* query, const void* 
  * IRIS_DECODE_OUT_LSE) into the final fp16 output:
  *   parts_o [num_parts, rows, D] fp32, parts_lse [num_parts, rows] fp32,
  *   output [rows, D] fp16, rows = B*Hq.
+ * A part with lse = -inf for a row contributes nothing to that row.
  * Used after an all-gather of per-GPU partials in split-context decode.  No
  * counterpart in the reference (split-KV is out of its scope, README.md:425).
  */
 IRIS_API int iris_b200_merge_lse_partials(const float* parts_o, const float* parts_lse, int32_t num_parts, int64_t rows,
                                  int32_t head_dim, void* output, void* stream);
+
+/*
+ * Same merge over one packed buffer, the layout a single all-gather of the
+ * per-GPU partials produces: part k occupies rows*(D+1) floats starting at
+ * parts + k*rows*(D+1), O [rows, D] first and lse [rows] after it.  A part
+ * whose lse is -inf for a row (a GPU that held none of that sequence's
+ * tokens) is skipped for that row; its O need not be written.  No counterpart
+ * in the reference.
+ */
+IRIS_API int iris_b200_merge_lse_packed(const float* parts, int32_t num_parts, int64_t rows, int32_t head_dim,
+                                        void* output, void* stream);
 
 #ifdef __cplusplus
 }

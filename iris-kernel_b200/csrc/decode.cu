@@ -706,18 +706,25 @@ __global__ void __launch_bounds__(D / 4) decode_combine_kernel(const DecodeParam
   }
 }
 
-// Merge of log-sum-exp partials from several producers (e.g. GPUs).
+// Merge of log-sum-exp partials from several producers (e.g. GPUs).  Part k
+// of row r: O at parts_o[k * o_stride + r * head_dim], lse at
+// parts_lse[k * lse_stride + r].  A part with lse = -inf holds none of the
+// row's tokens (a GPU without a split of that sequence) and is skipped, so
+// its O may be left unwritten.
 __global__ void merge_lse_kernel(const float* __restrict__ parts_o, const float* __restrict__ parts_lse,
-                                 int32_t num_parts, int64_t rows, int32_t head_dim, __half* __restrict__ out) {
+                                 int32_t num_parts, int64_t rows, int32_t head_dim, int64_t o_stride,
+                                 int64_t lse_stride, __half* __restrict__ out) {
   const int64_t row = blockIdx.x;
   if (row >= rows) return;
   float mx = kNegInf;
-  for (int k = 0; k < num_parts; ++k) mx = fmaxf(mx, parts_lse[k * rows + row]);
+  for (int k = 0; k < num_parts; ++k) mx = fmaxf(mx, parts_lse[k * lse_stride + row]);
   for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
     float acc = 0.f, ws = 0.f;
     for (int k = 0; k < num_parts; ++k) {
-      const float w = ex2(parts_lse[k * rows + row] - mx);
-      acc = fmaf(w, parts_o[(k * rows + row) * head_dim + d], acc);
+      const float lse = parts_lse[k * lse_stride + row];
+      if (lse == kNegInf) continue;
+      const float w = ex2(lse - mx);
+      acc = fmaf(w, parts_o[k * o_stride + row * head_dim + d], acc);
       ws += w;
     }
     out[row * head_dim + d] = __float2half_rn(acc / ws);
@@ -1052,15 +1059,37 @@ extern "C" int iris_b200_int4_paged_decode(const void* query, const void* k_data
   return e == cudaSuccess ? IRIS_OK : IRIS_ECUDA;
 }
 
-extern "C" int iris_b200_merge_lse_partials(const float* parts_o, const float* parts_lse, int32_t num_parts,
-                                            int64_t rows, int32_t head_dim, void* output, void* stream) {
+namespace {
+
+int launch_merge(const float* parts_o, const float* parts_lse, int32_t num_parts, int64_t rows, int32_t head_dim,
+                 int64_t o_stride, int64_t lse_stride, void* output, void* stream) {
   if (num_parts <= 0 || rows < 0 || head_dim <= 0 || parts_o == nullptr || parts_lse == nullptr || output == nullptr)
     return IRIS_EINVAL;
   if (rows == 0) return IRIS_OK;
+  if (rows > 0x7fffffff) return IRIS_EUNSUPPORTED;
   clear_stale_cuda_error();
   merge_lse_kernel<<<static_cast<unsigned>(rows), 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      parts_o, parts_lse, num_parts, rows, head_dim, static_cast<__half*>(output));
-  return cudaGetLastError() == cudaSuccess ? IRIS_OK : IRIS_ECUDA;
+      parts_o, parts_lse, num_parts, rows, head_dim, o_stride, lse_stride, static_cast<__half*>(output));
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    record_cuda_error(e, "merge_lse_kernel launch");
+    return IRIS_ECUDA;
+  }
+  return IRIS_OK;
+}
+
+}  // namespace
+
+extern "C" int iris_b200_merge_lse_partials(const float* parts_o, const float* parts_lse, int32_t num_parts,
+                                            int64_t rows, int32_t head_dim, void* output, void* stream) {
+  return launch_merge(parts_o, parts_lse, num_parts, rows, head_dim, rows * head_dim, rows, output, stream);
+}
+
+extern "C" int iris_b200_merge_lse_packed(const float* parts, int32_t num_parts, int64_t rows, int32_t head_dim,
+                                          void* output, void* stream) {
+  if (parts == nullptr) return IRIS_EINVAL;
+  const int64_t part = rows * (head_dim + 1);
+  return launch_merge(parts, parts + rows * head_dim, num_parts, rows, head_dim, part, part, output, stream);
 }
 
 extern "C" const char* iris_b200_last_cuda_error(void) { return iris::g_last_error; }

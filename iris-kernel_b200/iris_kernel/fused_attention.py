@@ -151,18 +151,26 @@ def fused_int4_paged_decode_attention(
 
 
 def decode_partial(query, k_data, v_data, k_scale, v_scale, block_table, seq_lens, *, page_size: int = 16,
-                   group_size: int = 32, softmax_scale: float | None = None):
+                   group_size: int = 32, softmax_scale: float | None = None, out: torch.Tensor | None = None,
+                   lse: torch.Tensor | None = None):
     """Decode attention in log-sum-exp form: returns ``(o, lse)`` with
     ``o [B, Hq, D]`` fp32 normalised over the given tokens and ``lse [B, Hq]``
     fp32 = log2(sum_l 2^(x_l)), x_l = softmax_scale * log2(e) * q.k_l.
     ``block_table`` may be a column slice (row stride > width) so that a
-    caller can attend over a page-aligned sub-range of each sequence."""
+    caller can attend over a page-aligned sub-range of each sequence.
+    ``out`` / ``lse`` (contiguous fp32 views, e.g. into an all-gather send
+    buffer) receive the result in place when given."""
     num_pages, num_kv_heads, head_dim = _check_cache(query, k_data, v_data, k_scale, v_scale, page_size, group_size)
     _validate_common_decode_inputs(query, block_table, seq_lens, num_pages=num_pages, num_kv_heads=num_kv_heads,
                                    page_size=page_size)
     _check_scales(query, k_data, v_data, k_scale, v_scale, num_pages, num_kv_heads, head_dim, page_size, group_size)
-    out = torch.empty(query.shape, dtype=torch.float32, device=query.device)
-    lse = torch.empty(query.shape[:2], dtype=torch.float32, device=query.device)
+    if out is None:
+        out = torch.empty(query.shape, dtype=torch.float32, device=query.device)
+    if lse is None:
+        lse = torch.empty(query.shape[:2], dtype=torch.float32, device=query.device)
+    for t, shape in ((out, query.shape), (lse, query.shape[:2])):
+        if t.shape != shape or t.dtype != torch.float32 or not t.is_contiguous() or t.device != query.device:
+            raise ValueError(f"partial outputs must be contiguous float32 {tuple(shape)} on the query's device")
     if query.shape[0]:
         _launch(query, k_data, v_data, k_scale, v_scale, block_table, seq_lens, out, lse, _lib.DECODE_OUT_LSE,
                 softmax_scale, page_size)
@@ -186,4 +194,25 @@ def merge_lse_partials(parts_o: torch.Tensor, parts_lse: torch.Tensor, output: t
             _lib.lib.iris_b200_merge_lse_partials(parts_o.data_ptr(), parts_lse.data_ptr(), P, B * Hq, D,
                                                   output.data_ptr(), _runtime.stream_ptr(parts_o.device)),
             "iris_b200_merge_lse_partials")
+    return output
+
+
+def merge_lse_packed(parts: torch.Tensor, num_parts: int, batch: int, num_q_heads: int, head_dim: int,
+                     output: torch.Tensor | None = None) -> torch.Tensor:
+    """Merge partials packed as one all-gather produces them: ``parts`` is a
+    flat fp32 buffer of ``num_parts`` blocks of ``batch*Hq*(D+1)`` floats,
+    each ``O [batch, Hq, D]`` then ``lse [batch, Hq]``.  Rows whose lse is
+    -inf in a block are ignored for that block."""
+    rows = batch * num_q_heads
+    if parts.dtype != torch.float32 or not parts.is_contiguous():
+        raise TypeError("parts must be a contiguous float32 buffer")
+    if parts.numel() != num_parts * rows * (head_dim + 1):
+        raise ValueError("parts must hold num_parts * batch * Hq * (D + 1) floats")
+    if output is None:
+        output = torch.empty((batch, num_q_heads, head_dim), dtype=torch.float16, device=parts.device)
+    with torch.cuda.device(parts.device):
+        _lib.check_status(
+            _lib.lib.iris_b200_merge_lse_packed(parts.data_ptr(), num_parts, rows, head_dim, output.data_ptr(),
+                                                _runtime.stream_ptr(parts.device)),
+            "iris_b200_merge_lse_packed")
     return output

@@ -1,0 +1,194 @@
+"""Decode over several GPUs, one process per GPU.
+
+The reference runs on one GPU only; these are the two ways this package
+spreads a decode batch over N GPUs of a node (torch.distributed, NCCL):
+
+* Sequence sharding (no collective).  Every GPU owns whole sequences: their
+  pages live in its own cache and it decodes them with
+  ``fused_int4_paged_decode_attention``; outputs stay where their sequences
+  live.  :func:`balance_sequences` assigns sequences to GPUs greedily,
+  longest first, by token count (the decode's cost is proportional to the
+  tokens read, not to the number of sequences).
+
+* Split-context (one all-gather).  Every sequence's context is cut into
+  page-aligned splits of ``split_tokens`` tokens and the splits are dealt out
+  to the GPUs (:func:`plan_split_context`); a GPU's cache holds the pages of
+  its own splits.  Each GPU runs one log-sum-exp-form decode over the tokens
+  it holds, packs ``(O, lse)`` into one buffer, all-gathers it, and merges the
+  N partials (:func:`split_context_decode`).  A GPU's splits of one sequence
+  are handed to the kernel as a single virtual sequence: attention does not
+  depend on the order of the tokens, and only a sequence's final split can end
+  in a partly filled page, which the concatenation keeps last.
+
+Nothing here moves KV pages between GPUs; remote data arrives only as the
+gathered partials, through NCCL.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from .fused_attention import decode_partial, merge_lse_packed
+
+
+def balance_sequences(seq_lens, world: int) -> list[list[int]]:
+    """Assign sequence indices to ``world`` GPUs, longest first, each to the
+    GPU with the fewest tokens so far (ties: lowest rank).  Every GPU's list
+    is returned in ascending order."""
+    if world <= 0:
+        raise ValueError("world must be positive")
+    lens = np.asarray(seq_lens, dtype=np.int64).reshape(-1)
+    load = np.zeros(world, dtype=np.int64)
+    owned: list[list[int]] = [[] for _ in range(world)]
+    for b in np.argsort(-lens, kind="stable"):
+        g = int(np.argmin(load))
+        owned[g].append(int(b))
+        load[g] += lens[b]
+    return [sorted(o) for o in owned]
+
+
+@dataclass
+class SplitPlan:
+    """What one GPU decodes in split-context mode.
+
+    ``seqs [Bl]``: global indices of the sequences this GPU holds tokens of
+    (ascending).  ``cols [Bl, W]``: for each of them the block-table columns
+    (page numbers within the sequence) of this GPU's splits, concatenated in
+    split order; entries past ``ceil(lens/page_size)`` are padding (column 0)
+    and never read.  ``lens [Bl]``: tokens this GPU holds per sequence.
+    ``batch``: the global batch size."""
+
+    rank: int
+    world: int
+    batch: int
+    seqs: np.ndarray
+    cols: np.ndarray
+    lens: np.ndarray
+
+    @property
+    def covers_every_sequence(self) -> bool:
+        return len(self.seqs) == self.batch
+
+
+def split_owner(seq: int, split: int, num_splits: int, world: int, mode: str) -> int:
+    """GPU that decodes split ``split`` (of ``num_splits``) of sequence ``seq``.
+
+    ``"strided"``: splits are dealt round-robin, starting one GPU further for
+    each sequence so that short sequences do not all land on GPU 0.
+    ``"contiguous"``: each GPU takes one contiguous block of a sequence's
+    splits (GPU g: splits [g*n/N, (g+1)*n/N))."""
+    if mode == "strided":
+        return (split + seq) % world
+    if mode == "contiguous":
+        return split * world // num_splits
+    raise ValueError(f"unknown split mode {mode!r}")
+
+
+def plan_split_context(seq_lens, world: int, rank: int, *, split_tokens: int = 8192, page_size: int = 16,
+                       mode: str = "strided") -> SplitPlan:
+    """The split-context plan of GPU ``rank`` for host-side ``seq_lens``."""
+    if not 0 <= rank < world:
+        raise ValueError("rank must be in [0, world)")
+    if split_tokens <= 0 or split_tokens % page_size:
+        raise ValueError("split_tokens must be a positive multiple of page_size")
+    lens = np.asarray(seq_lens, dtype=np.int64).reshape(-1)
+    if (lens <= 0).any():
+        raise ValueError("seq_lens must be positive")
+    pages_per_split = split_tokens // page_size
+    seqs, cols, counts = [], [], []
+    for b, L in enumerate(lens.tolist()):
+        n = -(-L // split_tokens)
+        mine = [j for j in range(n) if split_owner(b, j, n, world, mode) == rank]
+        if not mine:
+            continue
+        c = []
+        tokens = 0
+        for j in mine:
+            t0, t1 = j * split_tokens, min((j + 1) * split_tokens, L)
+            tokens += t1 - t0
+            c.append(np.arange(j * pages_per_split, j * pages_per_split + -(-(t1 - t0) // page_size)))
+        seqs.append(b)
+        cols.append(np.concatenate(c))
+        counts.append(tokens)
+    width = max((len(c) for c in cols), default=1)
+    table = np.zeros((len(cols), width), dtype=np.int64)
+    for i, c in enumerate(cols):
+        table[i, :len(c)] = c
+    return SplitPlan(rank, world, len(lens), np.asarray(seqs, dtype=np.int64), table,
+                     np.asarray(counts, dtype=np.int64))
+
+
+def local_block_table(plan: SplitPlan, block_table: torch.Tensor) -> torch.Tensor:
+    """This GPU's block table: row i lists the page ids of ``plan.seqs[i]``'s
+    local splits (gathered on the block table's device)."""
+    dev = block_table.device
+    if len(plan.seqs) == 0:
+        return torch.zeros((0, 1), dtype=block_table.dtype, device=dev)
+    rows = block_table.index_select(0, torch.from_numpy(plan.seqs).to(dev))
+    return torch.gather(rows, 1, torch.from_numpy(plan.cols).to(dev)).contiguous()
+
+
+def packed_size(batch: int, num_q_heads: int, head_dim: int) -> int:
+    """Floats in one GPU's packed partial: O [B, Hq, D] then lse [B, Hq]."""
+    return batch * num_q_heads * (head_dim + 1)
+
+
+def packed_views(buf: torch.Tensor, batch: int, num_q_heads: int, head_dim: int):
+    """``(o [B, Hq, D], lse [B, Hq])`` views of one packed partial."""
+    n = batch * num_q_heads * head_dim
+    return buf[:n].view(batch, num_q_heads, head_dim), buf[n:n + batch * num_q_heads].view(batch, num_q_heads)
+
+
+def pack_partials(o_local: torch.Tensor, lse_local: torch.Tensor, seqs, batch: int) -> torch.Tensor:
+    """Pack this GPU's partials of sequences ``seqs`` into a full-batch buffer;
+    sequences it holds no tokens of get lse = -inf (and O = 0)."""
+    _, hq, d = o_local.shape
+    buf = torch.zeros(packed_size(batch, hq, d), dtype=torch.float32, device=o_local.device)
+    o, lse = packed_views(buf, batch, hq, d)
+    lse.fill_(float("-inf"))
+    idx = torch.as_tensor(np.asarray(seqs, dtype=np.int64), device=o_local.device)
+    if idx.numel():
+        o.index_copy_(0, idx, o_local)
+        lse.index_copy_(0, idx, lse_local)
+    return buf
+
+
+def split_context_decode(query, k_data, v_data, k_scale, v_scale, block_table, plan: SplitPlan, *,
+                         group=None, page_size: int = 16, group_size: int = 32, softmax_scale=None,
+                         output: torch.Tensor | None = None) -> torch.Tensor:
+    """Split-context decode on this GPU, then all-gather + merge.
+
+    ``query [B, Hq, D]`` is the full batch (identical on every GPU);
+    ``block_table`` maps this GPU's splits to pages of its own cache
+    (``k_data`` ... ``v_scale``); entries of other GPUs' splits are not read.
+    Every GPU of ``group`` must call this with the same B, Hq, D.  Returns the
+    fp16 output ``[B, Hq, D]`` (the same on every GPU)."""
+    import torch.distributed as dist
+
+    batch, hq, d = query.shape
+    world = dist.get_world_size(group)
+    if plan.world != world or plan.batch != batch:
+        raise ValueError("plan does not match the process group or the batch")
+    dev = query.device
+    kw = dict(page_size=page_size, group_size=group_size, softmax_scale=softmax_scale)
+    if plan.covers_every_sequence:
+        # the decode writes straight into the send buffer
+        send = torch.empty(packed_size(batch, hq, d), dtype=torch.float32, device=dev)
+        o, lse = packed_views(send, batch, hq, d)
+        lens = torch.from_numpy(plan.lens.astype(np.int32)).to(dev)
+        decode_partial(query, k_data, v_data, k_scale, v_scale, local_block_table(plan, block_table), lens, out=o,
+                       lse=lse, **kw)
+    elif len(plan.seqs):
+        idx = torch.from_numpy(plan.seqs).to(dev)
+        lens = torch.from_numpy(plan.lens.astype(np.int32)).to(dev)
+        o_l, lse_l = decode_partial(query.index_select(0, idx).contiguous(), k_data, v_data, k_scale, v_scale,
+                                    local_block_table(plan, block_table), lens, **kw)
+        send = pack_partials(o_l, lse_l, plan.seqs, batch)
+    else:
+        send = pack_partials(query.new_empty((0, hq, d), dtype=torch.float32),
+                             query.new_empty((0, hq), dtype=torch.float32), plan.seqs, batch)
+    recv = torch.empty(world * send.numel(), dtype=torch.float32, device=dev)
+    dist.all_gather_into_tensor(recv, send, group=group)
+    return merge_lse_packed(recv, world, batch, hq, d, output)
