@@ -102,6 +102,10 @@ IRIS_DEV uint32_t lds32(uint32_t addr) {
   return v;
 }
 
+IRIS_DEV void sts32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
 // --------------------------------------------------------------- TMA copies
 // 1-D bulk copy global -> shared, completion signalled on `bar` (tx bytes).
 // Both addresses 16-byte aligned, bytes a multiple of 16.

@@ -38,6 +38,7 @@
 #include <cstdlib>
 #include <map>
 #include <mutex>
+#include <tuple>
 #include <utility>
 
 #include "common.cuh"
@@ -476,6 +477,86 @@ IRIS_DEV void finish_piece(const DecodeParams& p, WarpState<D, NT>& st, int b, i
   }
 }
 
+// The producer warp of a decode CTA: walks the CTA's page range, fetches
+// and validates page ids 32 at a time (all lanes, one chunk ahead), and lane 0
+// waits for free ring stages and issues, per page, one 4-D TMA copy per
+// tensor for the CTA's HB heads plus the page's two scale blocks.  Returns
+// once every copy it issued has landed (or a bounded wait gave up).
+template <int D>
+IRIS_DEV void run_producer(const CUtensorMap* kmap_p, const CUtensorMap* vmap_p, const DecodeParams& p,
+                           uint8_t* smem, int stage_bytes, int S, int HB, int hblk, int64_t u0, int64_t u1,
+                           int b_first, uint64_t* full, uint32_t full_u32, uint32_t empty_u32, int scale_block,
+                           int lane) {
+  using C = DecCfg<D>;
+  // All lanes fetch (and validate) page ids 32 at a time, one chunk ahead
+  // of lane 0, which waits for free stages and issues the copies.
+  if (lane == 0) {
+    prefetch_tensormap(kmap_p);
+    prefetch_tensormap(vmap_p);
+  }
+  const uint32_t tx = 2 * HB * C::kTileBytes + 2 * scale_block;
+  uint32_t issued = 0;
+  int s = 0;          // stage of the next page
+  uint32_t ph = 0;    // its ring pass parity
+  bool alive = true;
+  int b = b_first;
+  int64_t u = u0;
+  auto fetch_ids = [&](const int32_t* row, int64_t first, int64_t count) -> int32_t {
+    int32_t pid = 0;
+    if (lane < count) {
+      pid = row[first + lane];
+      if (pid < 0 || static_cast<int64_t>(pid) >= p.num_pages) {
+        set_error(p.err, IRIS_ERR_PAGE_ID);
+        pid = 0;  // stay in bounds; the error word makes the call fail
+      }
+    }
+    return pid;
+  };
+  while (alive && u < u1) {
+    const int64_t ps = p.prefix[b], pe = p.prefix[b + 1];
+    if (pe <= u) { ++b; continue; }
+    const int64_t hi = pe < u1 ? pe : u1;
+    const int32_t* bt_row = p.block_table + static_cast<int64_t>(b) * p.bt_stride;
+    int64_t chunk = u;
+    int32_t ids = fetch_ids(bt_row, chunk - ps, hi - chunk);
+    while (chunk < hi) {
+      const int n = static_cast<int>(hi - chunk < 32 ? hi - chunk : 32);
+      const int64_t next = chunk + n;
+      const int32_t ids_next = next < hi ? fetch_ids(bt_row, next - ps, hi - next) : 0;
+      for (int j = 0; j < n; ++j) {
+        const int32_t pid = __shfl_sync(0xffffffffu, ids, j);
+        if (lane == 0 && alive) {
+          if (!mbar_wait_bounded(empty_u32 + 8 * s, ph ^ 1, p.err)) {
+            alive = false;
+          } else {
+            uint8_t* st = smem + s * stage_bytes;
+            mbar_arrive_expect_tx(full + s, tx);
+            tma_load_4d(st, kmap_p, 0, 0, hblk * HB, pid, full + s);
+            tma_load_4d(st + HB * C::kTileBytes, vmap_p, 0, 0, hblk * HB, pid, full + s);
+            uint8_t* sc = st + 2 * HB * C::kTileBytes;
+            bulk_g2s(sc, p.k_scale + static_cast<int64_t>(pid) * scale_block, scale_block, full + s);
+            bulk_g2s(sc + scale_block, p.v_scale + static_cast<int64_t>(pid) * scale_block, scale_block, full + s);
+            ++issued;
+          }
+        }
+        if (++s == S) { s = 0; ph ^= 1; }
+      }
+      alive = __shfl_sync(0xffffffffu, alive, 0);
+      if (!alive) break;
+      ids = ids_next;
+      chunk = next;
+    }
+    u = hi;
+    ++b;
+  }
+  // drain: every copy this CTA issued has landed before it exits
+  if (lane == 0) {
+    const uint32_t last = issued;  // stages are issued in order, so the last S are [issued - S, issued)
+    const uint32_t first = last > static_cast<uint32_t>(S) ? last - S : 0;
+    for (uint32_t k = first; k < last; ++k) mbar_wait_bounded(full_u32 + 8 * (k % S), (k / S) & 1, p.err);
+  }
+}
+
 template <int D, int NT>
 __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ CUtensorMap kmap,
                                                         const __grid_constant__ CUtensorMap vmap,
@@ -511,74 +592,8 @@ __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ CUtensorM
   const uint32_t full_u32 = smem_u32(full), empty_u32 = smem_u32(empty);
 
   if (warp == HB) {
-    // ======================= producer warp =======================
-    // All lanes fetch (and validate) page ids 32 at a time, one chunk ahead
-    // of lane 0, which waits for free stages and issues the copies.
-    if (lane == 0) {
-      prefetch_tensormap(&kmap);
-      prefetch_tensormap(&vmap);
-    }
-    const uint32_t tx = 2 * HB * C::kTileBytes + 2 * scale_block;
-    uint32_t issued = 0;
-    int s = 0;          // stage of the next page
-    uint32_t ph = 0;    // its ring pass parity
-    bool alive = true;
-    int b = b_first;
-    int64_t u = u0;
-    auto fetch_ids = [&](const int32_t* row, int64_t first, int64_t count) -> int32_t {
-      int32_t pid = 0;
-      if (lane < count) {
-        pid = row[first + lane];
-        if (pid < 0 || static_cast<int64_t>(pid) >= p.num_pages) {
-          set_error(p.err, IRIS_ERR_PAGE_ID);
-          pid = 0;  // stay in bounds; the error word makes the call fail
-        }
-      }
-      return pid;
-    };
-    while (alive && u < u1) {
-      const int64_t ps = p.prefix[b], pe = p.prefix[b + 1];
-      if (pe <= u) { ++b; continue; }
-      const int64_t hi = pe < u1 ? pe : u1;
-      const int32_t* bt_row = p.block_table + static_cast<int64_t>(b) * p.bt_stride;
-      int64_t chunk = u;
-      int32_t ids = fetch_ids(bt_row, chunk - ps, hi - chunk);
-      while (chunk < hi) {
-        const int n = static_cast<int>(hi - chunk < 32 ? hi - chunk : 32);
-        const int64_t next = chunk + n;
-        const int32_t ids_next = next < hi ? fetch_ids(bt_row, next - ps, hi - next) : 0;
-        for (int j = 0; j < n; ++j) {
-          const int32_t pid = __shfl_sync(0xffffffffu, ids, j);
-          if (lane == 0 && alive) {
-            if (!mbar_wait_bounded(empty_u32 + 8 * s, ph ^ 1, p.err)) {
-              alive = false;
-            } else {
-              uint8_t* st = smem + s * stage_bytes;
-              mbar_arrive_expect_tx(full + s, tx);
-              tma_load_4d(st, &kmap, 0, 0, hblk * HB, pid, full + s);
-              tma_load_4d(st + HB * C::kTileBytes, &vmap, 0, 0, hblk * HB, pid, full + s);
-              uint8_t* sc = st + 2 * HB * C::kTileBytes;
-              bulk_g2s(sc, p.k_scale + static_cast<int64_t>(pid) * scale_block, scale_block, full + s);
-              bulk_g2s(sc + scale_block, p.v_scale + static_cast<int64_t>(pid) * scale_block, scale_block, full + s);
-              ++issued;
-            }
-          }
-          if (++s == S) { s = 0; ph ^= 1; }
-        }
-        alive = __shfl_sync(0xffffffffu, alive, 0);
-        if (!alive) break;
-        ids = ids_next;
-        chunk = next;
-      }
-      u = hi;
-      ++b;
-    }
-    // drain: every copy this CTA issued has landed before it exits
-    if (lane == 0) {
-      const uint32_t last = issued;  // stages are issued in order, so the last S are [issued - S, issued)
-      const uint32_t first = last > static_cast<uint32_t>(S) ? last - S : 0;
-      for (uint32_t k = first; k < last; ++k) mbar_wait_bounded(full_u32 + 8 * (k % S), (k / S) & 1, p.err);
-    }
+    run_producer<D>(&kmap, &vmap, p, smem, stage_bytes, S, HB, hblk, u0, u1, b_first, full, full_u32, empty_u32,
+                    scale_block, lane);
     return;
   }
 
@@ -658,6 +673,430 @@ __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ CUtensorM
     const bool complete = (ps >= u0) && (pe <= u1);
     const int64_t rec = static_cast<int64_t>(r) * 2 + (u == u0 ? 0 : 1);
     finish_piece<D, NT>(p, st, b, kvh, complete, rec, lane);
+    u = hi;
+    ++b;
+  }
+}
+
+// ------------------------------------------------- head-pair consumer path
+// For GQA groups of at most 4 query heads the MMA's 8 columns would be half
+// empty with one KV head per warp.  Here a warp owns HP = 8 / CW KV heads
+// and column c of every fragment belongs to KV head c / CW (query head
+// c % CW of it; CW = 4 or 2 columns per head, columns past the group size are
+// zero).  Scores: one accumulator per 32-dim group collects, head by head,
+// K_h . Q_h^T where head h's B operand is the query tile with every other
+// head's columns read as zeros, so each column receives only its own head's
+// products.  PV: O^T += V_h^T . P'_h^T with P' zeroed outside head h's
+// columns.  Softmax state, scale products and the rescaling of O are shared
+// by the HP heads, and O takes 32 registers for all of them.
+//
+// The query tile lives in shared memory (8 rows = columns x D halves, in the
+// k order of the QK MMAs, 16-byte chunks XOR-swizzled by row) and is read
+// with ldmatrix; lanes whose row belongs to another head point at a 256-byte
+// zero block instead.
+
+template <int D>
+struct PairState {
+  float o[D / 16][4];
+  float m[2];
+  float l[2];
+  float ncorr[D / 32][2];  // minus the bias correction per (group, column)
+};
+
+// Write the warp's query tile (heads kv0 .. kv0+HP-1 of sequence b) and
+// derive the bias corrections.  Lane (n = lane/4, t = lane%4) handles row n
+// and dims 8t..8t+7 of every 32-dim group.
+template <int D, int HP>
+IRIS_DEV void pair_load_query(PairState<D>& st, const __half* __restrict__ q_seq, int kv0, int qpk, uint32_t qtile,
+                              int lane) {
+  constexpr int CW = 8 / HP;
+  const int n = lane >> 2, t = lane & 3;
+  const int qi = n % CW;
+  const __half* qrow = q_seq + ((kv0 + n / CW) * qpk + qi) * D;
+  const uint32_t row = qtile + n * (2 * D);
+#pragma unroll
+  for (int g = 0; g < D / 32; ++g) {
+    uint4 raw = make_uint4(0, 0, 0, 0);
+    if (qi < qpk) raw = *reinterpret_cast<const uint4*>(qrow + g * 32 + t * 8);
+    const __half* e = reinterpret_cast<const __half*>(&raw);
+    const __half s16 = __float2half_rn(0.0625f);
+    __half eo[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) eo[i] = __hmul(e[2 * i + 1], s16);  // odd dims / 16 (exact)
+    // k-step 2g+sub: k = 2t, 2t+1 <- even dims 8t+2sub, 8t+2sub+4 (chunk 2ks);
+    //                k = 8+2t, 9+2t <- odd dims / 16 (chunk 2ks+1)
+#pragma unroll
+    for (int sub = 0; sub < 2; ++sub) {
+      const int ks = 2 * g + sub;
+      const uint32_t w0 = h2_as_u32(__halves2half2(e[2 * sub], e[2 * sub + 4]));
+      const uint32_t w1 = h2_as_u32(__halves2half2(eo[sub], eo[sub + 2]));
+      sts32(row + (((2 * ks) ^ n) << 4) + 4 * t, w0);
+      sts32(row + (((2 * ks + 1) ^ n) << 4) + 4 * t, w1);
+    }
+    float c = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      c += 1032.0f * __half2float(e[2 * i]);
+      c += 1152.0f * __half2float(eo[i]);
+    }
+    c += __shfl_xor_sync(0xffffffffu, c, 1);
+    c += __shfl_xor_sync(0xffffffffu, c, 2);
+    // column j of this lane's C fragment is row 2t + j of the tile
+    st.ncorr[g][0] = -__shfl_sync(0xffffffffu, c, (2 * t) * 4);
+    st.ncorr[g][1] = -__shfl_sync(0xffffffffu, c, (2 * t + 1) * 4);
+  }
+#pragma unroll
+  for (int i = 0; i < D / 16; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) st.o[i][j] = 0.f;
+  st.m[0] = st.m[1] = 0.f;  // replaced by the first page's maxima
+  st.l[0] = st.l[1] = 0.f;
+  __syncwarp();
+}
+
+// Scores of one page for the warp's HP heads: s[0..3] = S^T[token g8 / g8+8]
+// [column 2t / 2t+1] (unscaled logits).  ktile0: shared address of the first
+// head's K tile (heads follow at kTileBytes); qaddr[h]: this lane's ldmatrix
+// row address for head h's (masked) query tile, XOR 64*i selecting k-steps
+// 2i, 2i+1; ksc: the lane's head's column in the page's K scale block.
+template <int D, int HP>
+IRIS_DEV void pair_page_scores(const PairState<D>& st, uint32_t ktile0, const uint32_t (&qaddr)[HP], uint32_t ksc,
+                               int scale_stride, int lane, float (&s)[4]) {
+  constexpr int G = D / 32;
+  constexpr int kTile = kPage * D / 2;
+  const int g8 = lane >> 2;
+  float ks[2][G];
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    const uint32_t sp = ksc + (g8 + 8 * rr) * scale_stride;
+    if constexpr (G == 4) {
+      const uint2 u = lds64(sp);
+      const float2 a = __half22float2(u32_as_h2(u.x)), b = __half22float2(u32_as_h2(u.y));
+      ks[rr][0] = a.x; ks[rr][1] = a.y; ks[rr][2] = b.x; ks[rr][3] = b.y;
+    } else {
+      const float2 a = __half22float2(u32_as_h2(lds32(sp)));
+      ks[rr][0] = a.x; ks[rr][1] = a.y;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < G / 2; ++i) {
+    // groups 2i, 2i+1 of every head; the first MMA of a group reads its
+    // seed (minus the bias correction) straight from the state
+    float acc[2][4];
+#pragma unroll
+    for (int h = 0; h < HP; ++h) {
+      uint32_t kr[4];
+      ldmatrix_x4(kr, ktile0 + h * kTile + tile_lane_offset<D>(lane, i));
+#pragma unroll
+      for (int gg = 0; gg < 2; ++gg) {
+        uint32_t qb[4];  // (b0, b1) of k-steps 2g, 2g+1 for head h
+        ldmatrix_x4(qb, qaddr[h] ^ (64u * (2 * i + gg)));
+        const float(&nc)[2] = st.ncorr[2 * i + gg];
+        const float seed[4] = {nc[0], nc[1], nc[0], nc[1]};
+#pragma unroll
+        for (int sub = 0; sub < 2; ++sub) {
+          const uint32_t w0 = kr[2 * gg] >> (8 * sub), w1 = kr[2 * gg + 1] >> (8 * sub);
+          const uint32_t a[4] = {int4_lo_biased(w0), int4_lo_biased(w1), int4_hi_biased(w0), int4_hi_biased(w1)};
+          if (h == 0 && sub == 0)
+            mma_16816(acc[gg], a, qb[0], qb[1], seed);
+          else
+            mma_16816(acc[gg], a, qb[2 * sub], qb[2 * sub + 1], acc[gg]);
+        }
+      }
+    }
+#pragma unroll
+    for (int gg = 0; gg < 2; ++gg) {
+      const int g = 2 * i + gg;
+      if (g == 0) {
+        s[0] = ks[0][g] * acc[gg][0];
+        s[1] = ks[0][g] * acc[gg][1];
+        s[2] = ks[1][g] * acc[gg][2];
+        s[3] = ks[1][g] * acc[gg][3];
+      } else {
+        s[0] = fmaf(ks[0][g], acc[gg][0], s[0]);
+        s[1] = fmaf(ks[0][g], acc[gg][1], s[1]);
+        s[2] = fmaf(ks[1][g], acc[gg][2], s[2]);
+        s[3] = fmaf(ks[1][g], acc[gg][3], s[3]);
+      }
+    }
+  }
+}
+
+// O^T += V_h^T P'_h^T over the warp's heads for one page.  p[0..3] are the
+// lane's probabilities in the score layout; vsc is the column of the lane's
+// B-operand head (column g8) in the V scale block; tokens >= `valid` get a
+// zero V scale when MASK.
+template <int D, int HP, bool MASK>
+IRIS_DEV void pair_page_pv(PairState<D>& st, uint32_t vtile0, uint32_t vsc, int scale_stride, int valid,
+                           const float (&p)[4], int lane) {
+  constexpr int G = D / 32;
+  constexpr int CW = 8 / HP;
+  constexpr int kTile = kPage * D / 2;
+  const int t = lane & 3;
+  const int hb = (lane >> 2) / CW;  // head of this lane's B column
+  uint32_t sv01[G], sv89[G];
+  {
+    uint32_t raw[4][G / 2];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int tok = 2 * t + (k & 1) + 8 * (k >> 1);
+      const uint32_t sp = vsc + tok * scale_stride;
+      const bool ok = !MASK || tok < valid;
+      if constexpr (G == 4) {
+        const uint2 u = lds64(sp);
+        raw[k][0] = ok ? u.x : 0u;
+        raw[k][1] = ok ? u.y : 0u;
+      } else {
+        const uint32_t u = lds32(sp);
+        raw[k][0] = ok ? u : 0u;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < G / 2; ++j) {
+      sv01[2 * j] = prmt(raw[0][j], raw[1][j], 0x5410);
+      sv01[2 * j + 1] = prmt(raw[0][j], raw[1][j], 0x7632);
+      sv89[2 * j] = prmt(raw[2][j], raw[3][j], 0x5410);
+      sv89[2 * j + 1] = prmt(raw[2][j], raw[3][j], 0x7632);
+    }
+  }
+  const uint32_t pb0 = movmatrix_trans(h2_as_u32(__floats2half2_rn(p[0], p[1])));
+  const uint32_t pb1 = movmatrix_trans(h2_as_u32(__floats2half2_rn(p[2], p[3])));
+#pragma unroll
+  for (int h = 0; h < HP; ++h) {
+    const uint32_t q0 = hb == h ? pb0 : 0u, q1 = hb == h ? pb1 : 0u;
+#pragma unroll
+    for (int i = 0; i < G / 2; ++i) {
+      uint32_t r[4];
+      ldmatrix_x4_trans(r, vtile0 + h * kTile + tile_lane_offset<D>(lane, i));
+#pragma unroll
+      for (int gg = 0; gg < 2; ++gg) {
+        const int g = 2 * i + gg;
+        const uint32_t wa = r[2 * gg], wb = r[2 * gg + 1];
+        const uint32_t b0 = h2_as_u32(__hmul2(u32_as_h2(q0), u32_as_h2(sv01[g])));
+        const uint32_t b1 = h2_as_u32(__hmul2(u32_as_h2(q1), u32_as_h2(sv89[g])));
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const uint32_t xa = wa >> (8 * jj), xb = wb >> (8 * jj);
+          const uint32_t a[4] = {int4_lo_exact(xa), int4_hi_exact(xa), int4_lo_exact(xb), int4_hi_exact(xb)};
+          mma_16816(st.o[2 * g + jj], a, b0, b1, st.o[2 * g + jj]);
+        }
+      }
+    }
+  }
+}
+
+// One page with an online-softmax update whose running maximum may be stale
+// by up to 8 (log2 units): y = scale*s - m is computed with one FFMA, and
+// only when some y exceeds 8 (probabilities would pass 2^8) does the warp
+// find the column maxima, raise m to them and rescale O and l.  Otherwise
+// p = 2^y <= 256, still exact enough in fp16 for the PV product, and the
+// max reduction and the rescale are skipped.  `first` marks a piece's first
+// page: m then starts at that page's maxima (O and l are still zero).
+template <int D, int HP, bool MASK>
+IRIS_DEV void pair_process_page(PairState<D>& st, uint32_t base, uint32_t k_off, uint32_t v_off,
+                                 const uint32_t (&qaddr)[HP], uint32_t ks_off, uint32_t vs_off, int scale_stride,
+                                 int valid, float scale_log2, bool first, int lane) {
+  const int g8 = lane >> 2;
+  float s[4];
+  pair_page_scores<D, HP>(st, base + k_off, qaddr, base + ks_off, scale_stride, lane, s);
+  float y[4];
+  y[0] = fmaf(s[0], scale_log2, -st.m[0]);
+  y[1] = fmaf(s[1], scale_log2, -st.m[1]);
+  y[2] = fmaf(s[2], scale_log2, -st.m[0]);
+  y[3] = fmaf(s[3], scale_log2, -st.m[1]);
+  if (MASK) {
+    if (g8 >= valid) y[0] = y[1] = kNegInf;
+    if (g8 + 8 >= valid) y[2] = y[3] = kNegInf;
+  }
+  float mx0 = fmaxf(y[0], y[2]), mx1 = fmaxf(y[1], y[3]);
+  if (__any_sync(0xffffffffu, first || fmaxf(mx0, mx1) > 8.0f)) {
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+    }
+    // raise each column's maximum by inc (never lower it after the first page)
+    const float inc0 = first ? mx0 : fmaxf(mx0, 0.f), inc1 = first ? mx1 : fmaxf(mx1, 0.f);
+    st.m[0] += inc0;
+    st.m[1] += inc1;
+    y[0] -= inc0;
+    y[1] -= inc1;
+    y[2] -= inc0;
+    y[3] -= inc1;
+    if (!first) {
+      const float c0 = ex2(-inc0), c1 = ex2(-inc1);
+#pragma unroll
+      for (int i = 0; i < D / 16; ++i) {
+        st.o[i][0] *= c0;
+        st.o[i][1] *= c1;
+        st.o[i][2] *= c0;
+        st.o[i][3] *= c1;
+      }
+      st.l[0] *= c0;
+      st.l[1] *= c1;
+    }
+  }
+  float pr[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) pr[k] = ex2(y[k]);  // ex2(-inf) = 0 for masked tokens
+  st.l[0] += pr[0] + pr[2];
+  st.l[1] += pr[1] + pr[3];
+  pair_page_pv<D, HP, MASK>(st, base + v_off, base + vs_off, scale_stride, valid, pr, lane);
+}
+
+// Finish a (sequence piece, head group): column c of the fragments is query
+// head (kv0 + c / CW) * qpk + c % CW.
+template <int D, int HP>
+IRIS_DEV void pair_finish_piece(const DecodeParams& p, PairState<D>& st, int b, int kv0, bool complete, int64_t rec,
+                                int lane) {
+  constexpr int CW = 8 / HP;
+  const int g8 = lane >> 2, t = lane & 3;
+  float l0 = st.l[0], l1 = st.l[1];
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+  }
+  const float inv[2] = {1.0f / l0, 1.0f / l1};
+  const float lse[2] = {st.m[0] + lg2(l0), st.m[1] + lg2(l1)};
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int c = 2 * t + j;
+    if (c % CW >= p.qpk) continue;
+    const int qh = (kv0 + c / CW) * p.qpk + c % CW;
+#pragma unroll
+    for (int g = 0; g < D / 32; ++g) {
+      const float v0 = st.o[2 * g][j] * inv[j];
+      const float v1 = st.o[2 * g][2 + j] * inv[j];
+      const float v2 = st.o[2 * g + 1][j] * inv[j];
+      const float v3 = st.o[2 * g + 1][2 + j] * inv[j];
+      const int d = 32 * g + 4 * g8;
+      if (complete && p.out_mode == IRIS_DECODE_OUT_FP16) {
+        __half* dst = static_cast<__half*>(p.out) + (static_cast<int64_t>(b) * p.hq + qh) * D + d;
+        uint2 u;
+        u.x = h2_as_u32(__floats2half2_rn(v0, v1));
+        u.y = h2_as_u32(__floats2half2_rn(v2, v3));
+        *reinterpret_cast<uint2*>(dst) = u;
+      } else {
+        float* dst = complete ? static_cast<float*>(p.out) + (static_cast<int64_t>(b) * p.hq + qh) * D + d
+                              : p.rec_o + (rec * p.hq + qh) * D + d;
+        *reinterpret_cast<float4*>(dst) = make_float4(v0, v1, v2, v3);
+      }
+    }
+    if (g8 == 0) {
+      if (complete) {
+        if (p.out_mode == IRIS_DECODE_OUT_LSE) p.out_lse[static_cast<int64_t>(b) * p.hq + qh] = lse[j];
+      } else {
+        p.rec_lse[rec * p.hq + qh] = lse[j];
+      }
+    }
+  }
+}
+
+// Decode CTA with HB/HP consumer warps of HP heads each + 1 producer warp.
+// Shared memory: the stage ring, the full/empty barriers, a 256-byte zero
+// block, then one 2*8*D-byte query tile per consumer warp.
+template <int D, int HP>
+__global__ void __maxnreg__(128) decode_pair_kernel(const __grid_constant__ CUtensorMap kmap,
+                                                             const __grid_constant__ CUtensorMap vmap,
+                                                             const DecodeParams p) {
+  using C = DecCfg<D>;
+  constexpr int CW = 8 / HP;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  const int hblk = blockIdx.x;
+  const int r = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int HB = p.hb;
+  const int NW = HB / HP;  // consumer warps
+  const int S = p.stages;
+  const int U = p.meta[0], R = p.meta[1];
+  if (r >= R) return;  // uniform per CTA
+
+  const int scale_block = kPage * p.hkv * C::kGroups * 2;
+  const int stage_bytes = ((2 * HB * C::kTileBytes + 2 * scale_block) + 1023) & ~1023;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * stage_bytes);
+  uint64_t* empty = full + S;
+  uint8_t* zero_blk = smem + ((S * stage_bytes + 16 * S + 255) & ~255);
+  uint8_t* qtiles = zero_blk + 256;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, NW);
+    }
+    fence_barrier_init();
+  }
+  if (threadIdx.x < 64) reinterpret_cast<uint32_t*>(zero_blk)[threadIdx.x] = 0u;
+  __syncthreads();
+
+  const int64_t u0 = range_start(r, U, R), u1 = range_start(r + 1, U, R);
+  const int b_first = p.range_seq[r];
+  const uint32_t full_u32 = smem_u32(full), empty_u32 = smem_u32(empty);
+
+  if (warp == NW) {
+    run_producer<D>(&kmap, &vmap, p, smem, stage_bytes, S, HB, hblk, u0, u1, b_first, full, full_u32, empty_u32,
+                    scale_block, lane);
+    return;
+  }
+
+  // ========================= consumer warps =========================
+  const int kv0 = hblk * HB + warp * HP;  // first KV head of this warp
+  const int g8 = lane >> 2, t = lane & 3;
+  PairState<D> st;
+  const uint32_t ring = smem_u32(smem);
+  const uint32_t qtile = smem_u32(qtiles) + warp * (16 * D);
+  // ldmatrix row addresses of the masked query tile per head: lane l reads
+  // row (l & 7) of matrix (l >> 3); rows of other heads read the zero block
+  uint32_t qaddr[HP];
+  {
+    const int row = lane & 7, x = (lane >> 3) ^ row;
+#pragma unroll
+    for (int h = 0; h < HP; ++h)
+      qaddr[h] = (row / CW == h ? qtile + row * (2 * D) : smem_u32(zero_blk)) | (x << 4);
+  }
+  const uint32_t k_off = warp * HP * C::kTileBytes, v_off = (HB + warp * HP) * C::kTileBytes;
+  const uint32_t ks_off = 2 * HB * C::kTileBytes + (kv0 + (2 * t) / CW) * C::kGroups * 2;
+  const uint32_t vs_off = 2 * HB * C::kTileBytes + scale_block + (kv0 + g8 / CW) * C::kGroups * 2;
+  const int scale_stride = p.hkv * C::kGroups * 2;
+  int s = 0;
+  uint32_t ph = 0;
+  uint32_t stage = ring;
+  int b = b_first;
+  int64_t u = u0;
+  while (u < u1) {
+    const int64_t ps = p.prefix[b], pe = p.prefix[b + 1];
+    if (pe <= u) { ++b; continue; }
+    const int64_t hi = pe < u1 ? pe : u1;
+    const int L = min(p.seq_lens[b], p.max_pages * kPage);
+    __syncwarp();  // the previous piece's ldmatrix reads of the tile are done
+    pair_load_query<D, HP>(st, p.query + static_cast<int64_t>(b) * p.hq * D, kv0, p.qpk, qtile, lane);
+    int valid = L - static_cast<int>(u - ps) * kPage;  // tokens left from this page on
+    bool first = true;
+    for (int64_t left = hi - u; left > 0; --left) {
+      if (!mbar_wait_bounded(full_u32 + 8 * s, ph, p.err)) return;
+      if (valid >= kPage)
+        pair_process_page<D, HP, false>(st, stage, k_off, v_off, qaddr, ks_off, vs_off, scale_stride, valid,
+                                        p.scale_log2, first, lane);
+      else
+        pair_process_page<D, HP, true>(st, stage, k_off, v_off, qaddr, ks_off, vs_off, scale_stride, valid,
+                                       p.scale_log2, first, lane);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty_u32 + 8 * s);
+      first = false;
+      valid -= kPage;
+      if (++s == S) {
+        s = 0;
+        ph ^= 1;
+        stage = ring;
+      } else {
+        stage += stage_bytes;
+      }
+    }
+    const bool complete = (ps >= u0) && (pe <= u1);
+    const int64_t rec = static_cast<int64_t>(r) * 2 + (u == u0 ? 0 : 1);
+    pair_finish_piece<D, HP>(p, st, b, kv0, complete, rec, lane);
     u = hi;
     ++b;
   }
@@ -780,27 +1219,63 @@ bool make_kv_map(CUtensorMap* map, const void* base, int D, int hkv, int hb, int
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int pick_hb(int hkv);
+using DecodeKernelFn = void (*)(CUtensorMap, CUtensorMap, DecodeParams);
 
-// KV heads per CTA: the largest power of two <= max_hb dividing Hkv.
-// IRIS_DECODE_MAX_HB (1, 2, 4 or 8) overrides the default of 4 for tuning.
-int max_hb() {
-  static int v = [] {
-    const char* e = getenv("IRIS_DECODE_MAX_HB");
-    int x = e ? atoi(e) : 4;
-    return (x == 1 || x == 2 || x == 4 || x == 8) ? x : 4;
-  }();
-  return v;
+// KV heads per consumer warp: groups of at most 4 query heads share a warp's
+// 8 MMA columns between 2 (3-4 query heads) or 4 (1-2) KV heads
+// (decode_pair_kernel); larger groups get one KV head per warp
+// (decode_kernel).
+int heads_per_warp(int qpk, int hkv) {
+  if (qpk > 4) return 1;
+  int hp = qpk <= 2 ? 4 : 2;
+  while (hp > 1 && hkv % hp != 0) hp >>= 1;
+  return hp;
 }
 
-int pick_hb(int hkv) {
-  for (int hb = max_hb(); hb >= 1; hb >>= 1)
-    if (hkv % hb == 0) return hb;
-  return 1;
+// Cap on KV heads per CTA.  IRIS_DECODE_MAX_HB (1, 2, 4 or 8) overrides the
+// defaults (8 with head groups per warp, else 4) for tuning.
+int max_hb(int dflt) {
+  static int v = [] {
+    const char* e = getenv("IRIS_DECODE_MAX_HB");
+    int x = e ? atoi(e) : 0;
+    return (x == 1 || x == 2 || x == 4 || x == 8) ? x : 0;
+  }();
+  return v ? v : dflt;
+}
+
+// The CTA shape of one decode problem.
+struct Plan {
+  DecodeKernelFn fn;
+  int hp;    // KV heads per consumer warp
+  int hb;    // KV heads per CTA (one TMA box)
+  int nw;    // consumer warps = hb / hp
+  int pair;  // decode_pair_kernel (query tiles in shared memory)
+};
+
+Plan make_plan(int D, int qpk, int hkv) {
+  Plan pl;
+  pl.hp = heads_per_warp(qpk, hkv);
+  pl.pair = pl.hp > 1;
+  const int cap = max_hb(pl.pair ? 8 : 4);
+  pl.hb = pl.hp;
+  for (int hb = cap; hb >= pl.hp; hb >>= 1)
+    if (hkv % hb == 0 && hb % pl.hp == 0) {
+      pl.hb = hb;
+      break;
+    }
+  pl.nw = pl.hb / pl.hp;
+  if (D == 128) {
+    pl.fn = pl.hp == 4 ? decode_pair_kernel<128, 4> : pl.hp == 2 ? decode_pair_kernel<128, 2>
+          : qpk <= 8   ? decode_kernel<128, 1>      : decode_kernel<128, 2>;
+  } else {
+    pl.fn = pl.hp == 4 ? decode_pair_kernel<64, 4> : pl.hp == 2 ? decode_pair_kernel<64, 2>
+          : qpk <= 8   ? decode_kernel<64, 1>      : decode_kernel<64, 2>;
+  }
+  return pl;
 }
 
 struct LaunchShape {
-  int hb, nhb, stages, stage_bytes, smem, ranges, max_ranges;
+  int stages, stage_bytes, smem, ranges, max_ranges;
 };
 
 int stage_bytes_for(int D, int hkv, int hb) {
@@ -809,7 +1284,13 @@ int stage_bytes_for(int D, int hkv, int hb) {
   return ((2 * hb * tile + 2 * scale_block) + 1023) & ~1023;
 }
 
-int smem_for(int stages, int stage_bytes) { return stages * stage_bytes + 2 * stages * 8 + 1024; }
+// Ring + barriers (+ zero block and query tiles for the pair kernel) + the
+// slack for aligning the dynamic shared memory base to 1 KB.
+int smem_for(const Plan& pl, int D, int stages, int stage_bytes) {
+  int bytes = stages * stage_bytes + 2 * stages * 8;
+  if (pl.pair) bytes = ((bytes + 255) & ~255) + 256 + pl.nw * 16 * D;
+  return bytes + 1024;
+}
 
 int device_sms(int device) {
   static std::mutex mu;
@@ -826,58 +1307,57 @@ int device_sms(int device) {
   return sms;
 }
 
-// Upper bound on the number of ranges (sizes the workspace): at most
-// 16 consumer warps' worth of CTAs per SM.
-int max_ranges_for(int hkv, int sms) {
-  const int hb = pick_hb(hkv);
-  const int nhb = hkv / hb;
-  const int ctas = 16 / hb < 1 ? 1 : 16 / hb;
-  const int r = sms * ctas / nhb;
+int target_ctas_per_sm(const Plan& pl) { return 16 / pl.nw < 1 ? 1 : 16 / pl.nw; }
+
+// Upper bound on the number of ranges (sizes the workspace): at most 16
+// consumer warps' worth of CTAs per SM.
+int max_ranges_for(int qpk, int hkv, int sms) {
+  const Plan pl = make_plan(128, qpk, hkv);
+  const int r = sms * target_ctas_per_sm(pl) / (hkv / pl.hb);
   return r < 1 ? 1 : r;
 }
 
 // The dynamic shared memory limit is a per-kernel attribute shared by every
 // shape, so it only ever grows (a smaller shape must not lower it under a
 // larger cached one).
-template <int D, int NT>
-cudaError_t ensure_smem_attr(int device, int smem) {
+cudaError_t ensure_smem_attr(DecodeKernelFn fn, int device, int smem) {
   static std::mutex mu;
-  static std::map<int, int> set_to;
+  static std::map<std::pair<const void*, int>, int> set_to;
   std::lock_guard<std::mutex> lock(mu);
-  int& cur = set_to[device];
+  int& cur = set_to[std::make_pair(reinterpret_cast<const void*>(fn), device)];
   if (smem <= cur) return cudaSuccess;
-  const cudaError_t e = cudaFuncSetAttribute(decode_kernel<D, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  const cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e == cudaSuccess) cur = smem;
   return e;
 }
 
-// Computed once per (D, NT, Hkv, device): later calls make no attribute or
+// Computed once per (kernel, Hkv, device): later calls make no attribute or
 // occupancy queries, so the entry point can be captured in a CUDA graph
 // after its first (uncaptured) call.
-template <int D, int NT>
-LaunchShape compute_launch_shape(int hkv, int device) {
+LaunchShape compute_launch_shape(const Plan& pl, int D, int qpk, int hkv, int device) {
   LaunchShape s;
   const int sms = device_sms(device);
-  s.hb = pick_hb(hkv);
-  s.nhb = hkv / s.hb;
-  s.stage_bytes = stage_bytes_for(D, hkv, s.hb);
-  s.max_ranges = max_ranges_for(hkv, sms);
-  const int threads = (s.hb + 1) * 32;
-  int target = 16 / s.hb < 1 ? 1 : 16 / s.hb;
-  for (; target >= 1; --target) {
-    int stages = (kSmemBudgetPerSm / target - 1024 - 256) / s.stage_bytes;
+  const int nhb = hkv / pl.hb;
+  s.stage_bytes = stage_bytes_for(D, hkv, pl.hb);
+  s.max_ranges = max_ranges_for(qpk, hkv, sms);
+  const int threads = (pl.nw + 1) * 32;
+  for (int target = target_ctas_per_sm(pl); target >= 1; --target) {
+    const int fixed = smem_for(pl, D, 0, s.stage_bytes);
+    int stages = (kSmemBudgetPerSm / target - fixed - 256) / (s.stage_bytes + 16);
     stages = stages < 2 ? 2 : (stages > 10 ? 10 : stages);
-    const int smem = smem_for(stages, s.stage_bytes);
+    const int smem = smem_for(pl, D, stages, s.stage_bytes);
     int occ = 0;
-    if (ensure_smem_attr<D, NT>(device, smem) != cudaSuccess ||
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel<D, NT>, threads, smem) != cudaSuccess) {
+    if (ensure_smem_attr(pl.fn, device, smem) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, reinterpret_cast<const void*>(pl.fn), threads, smem) !=
+            cudaSuccess) {
       cudaGetLastError();
       occ = 0;
     }
     if (occ >= target || target == 1) {
       s.stages = stages;
       s.smem = smem;
-      int ranges = sms * (occ < target ? (occ > 0 ? occ : 1) : target) / s.nhb;
+      int ranges = sms * (occ < target ? (occ > 0 ? occ : 1) : target) / nhb;
       ranges = ranges < 1 ? 1 : ranges;
       s.ranges = ranges > s.max_ranges ? s.max_ranges : ranges;
       break;
@@ -886,15 +1366,14 @@ LaunchShape compute_launch_shape(int hkv, int device) {
   return s;
 }
 
-template <int D, int NT>
-LaunchShape launch_shape(int hkv, int device) {
+LaunchShape launch_shape(const Plan& pl, int D, int qpk, int hkv, int device) {
   static std::mutex mu;
-  static std::map<std::pair<int, int>, LaunchShape> cache;
+  static std::map<std::tuple<const void*, int, int>, LaunchShape> cache;
   std::lock_guard<std::mutex> lock(mu);
-  const auto key = std::make_pair(hkv, device);
+  const auto key = std::make_tuple(reinterpret_cast<const void*>(pl.fn), hkv, device);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
-  const LaunchShape s = compute_launch_shape<D, NT>(hkv, device);
+  const LaunchShape s = compute_launch_shape(pl, D, qpk, hkv, device);
   cache[key] = s;
   return s;
 }
@@ -928,11 +1407,11 @@ Workspace carve(void* base, int batch, int hq, int D, int ranges) {
   return w;
 }
 
-template <int D, int NT>
-cudaError_t launch_decode(const CUtensorMap& km, const CUtensorMap& vm, DecodeParams p, int device,
+template <int D>
+cudaError_t launch_decode(const Plan& pl, const CUtensorMap& km, const CUtensorMap& vm, DecodeParams p, int device,
                           cudaStream_t stream, int32_t ranges_cap) {
-  const LaunchShape ls = launch_shape<D, NT>(p.hkv, device);
-  p.hb = ls.hb;
+  const LaunchShape ls = launch_shape(pl, D, p.qpk, p.hkv, device);
+  p.hb = pl.hb;
   p.stages = ls.stages;
   const int32_t ranges = ls.ranges < ranges_cap ? ls.ranges : ranges_cap;
   cudaError_t e;
@@ -944,16 +1423,15 @@ cudaError_t launch_decode(const CUtensorMap& km, const CUtensorMap& vm, DecodePa
     record_cuda_error(e, "decode_plan_kernel launch");
     return e;
   }
-  auto kern = decode_kernel<D, NT>;
-  e = ensure_smem_attr<D, NT>(device, ls.smem);  // no-op once raised
+  e = ensure_smem_attr(pl.fn, device, ls.smem);  // no-op once raised
   if (e != cudaSuccess) {
     record_cuda_error(e, "cudaFuncSetAttribute(max dynamic smem)");
     return e;
   }
   // head blocks of one range are adjacent in launch order: they share the
   // page's scale sectors and DRAM rows
-  dim3 grid(ls.nhb, ranges);
-  kern<<<grid, (ls.hb + 1) * 32, ls.smem, stream>>>(km, vm, p);
+  dim3 grid(p.hkv / pl.hb, ranges);
+  pl.fn<<<grid, (pl.nw + 1) * 32, ls.smem, stream>>>(km, vm, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) {
     record_cuda_error(e, "decode_kernel launch");
@@ -971,7 +1449,10 @@ cudaError_t launch_decode(const CUtensorMap& km, const CUtensorMap& vm, DecodePa
 extern "C" size_t iris_b200_decode_workspace_bytes(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
                                                    int32_t head_dim, int32_t device) {
   if (batch <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || (head_dim != 64 && head_dim != 128)) return 0;
-  return carve(nullptr, batch, num_q_heads, head_dim, max_ranges_for(num_kv_heads, device_sms(device))).bytes;
+  if (num_q_heads % num_kv_heads != 0) return 0;
+  return carve(nullptr, batch, num_q_heads, head_dim,
+               max_ranges_for(num_q_heads / num_kv_heads, num_kv_heads, device_sms(device)))
+      .bytes;
 }
 
 extern "C" int iris_b200_int4_paged_decode(const void* query, const void* k_data, const void* v_data,
@@ -1008,14 +1489,14 @@ extern "C" int iris_b200_int4_paged_decode(const void* query, const void* k_data
     record_cuda_error(e0, "cudaGetDevice");
     return IRIS_ECUDA;
   }
-  const int32_t max_ranges = max_ranges_for(num_kv_heads, device_sms(device));
+  const int32_t max_ranges = max_ranges_for(qpk, num_kv_heads, device_sms(device));
   const Workspace ws = carve(workspace, batch, num_q_heads, head_dim, max_ranges);
   if (workspace_bytes < ws.bytes) return IRIS_EWORKSPACE;
 
   CUtensorMap km, vm;
-  const int hb = pick_hb(num_kv_heads);
-  if (!make_kv_map(&km, k_data, head_dim, num_kv_heads, hb, num_pages) ||
-      !make_kv_map(&vm, v_data, head_dim, num_kv_heads, hb, num_pages)) {
+  const Plan plan = make_plan(head_dim, qpk, num_kv_heads);
+  if (!make_kv_map(&km, k_data, head_dim, num_kv_heads, plan.hb, num_pages) ||
+      !make_kv_map(&vm, v_data, head_dim, num_kv_heads, plan.hb, num_pages)) {
     snprintf(iris::g_last_error, sizeof(iris::g_last_error), "cuTensorMapEncodeTiled failed (D=%d Hkv=%d pages=%lld)", head_dim,
              num_kv_heads, static_cast<long long>(num_pages));
     return IRIS_ECUDA;
@@ -1049,13 +1530,8 @@ extern "C" int iris_b200_int4_paged_decode(const void* query, const void* k_data
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
-  if (head_dim == 128) {
-    e = qpk <= 8 ? launch_decode<128, 1>(km, vm, p, device, s, max_ranges)
-                 : launch_decode<128, 2>(km, vm, p, device, s, max_ranges);
-  } else {
-    e = qpk <= 8 ? launch_decode<64, 1>(km, vm, p, device, s, max_ranges)
-                 : launch_decode<64, 2>(km, vm, p, device, s, max_ranges);
-  }
+  e = head_dim == 128 ? launch_decode<128>(plan, km, vm, p, device, s, max_ranges)
+                      : launch_decode<64>(plan, km, vm, p, device, s, max_ranges);
   return e == cudaSuccess ? IRIS_OK : IRIS_ECUDA;
 }
 
