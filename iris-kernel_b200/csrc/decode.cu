@@ -55,6 +55,7 @@ const char* record_cuda_error(cudaError_t e, const char* where) {
 cudaError_t clear_stale_cuda_error() { return cudaGetLastError(); }
 
 constexpr int kPage = 16;
+constexpr int kMinPagesPerRange = 4;  // ranges hold at least this many pages
 #define kNegInf (-__int_as_float(0x7f800000))
 
 struct DecodeParams {
@@ -68,9 +69,8 @@ struct DecodeParams {
   float* out_lse;            // [B,Hq] (LSE mode)
   float* rec_o;              // [R, 2, Hq, D]
   float* rec_lse;            // [R, 2, Hq]
-  const int32_t* prefix;     // [B+1] page prefix sums
-  const int32_t* range_seq;  // [R] first sequence of each range
-  const int32_t* meta;       // [0] total pages U, [1] ranges in use
+  const int32_t* prefix;     // [B+1] page prefix sums (written by the leader CTA for the combine)
+  const int32_t* meta;       // [0] total pages U, [1] ranges in use (likewise)
   int32_t* err;
   int64_t num_pages;
   int32_t batch, hq, hkv, max_pages;
@@ -91,31 +91,42 @@ struct DecCfg {
 IRIS_DEV int64_t range_start(int64_t r, int64_t U, int64_t R) { return r * U / R; }
 IRIS_DEV int64_t range_of_page(int64_t u, int64_t U, int64_t R) { return ((u + 1) * R - 1) / U; }
 
-// ------------------------------------------------------------- plan kernel
-// Single CTA: page counts and prefix sums of the sequences, validation of
-// the lengths, and the first sequence of every range.
-__global__ void __launch_bounds__(1024) decode_plan_kernel(const int32_t* __restrict__ seq_lens, int32_t batch,
-                                                           int32_t max_pages, int32_t ranges, int32_t min_pages,
-                                                           int32_t* __restrict__ prefix,
-                                                           int32_t* __restrict__ range_seq,
-                                                           int32_t* __restrict__ meta, int32_t* err) {
-  __shared__ int32_t warp_tot[32];
-  __shared__ int32_t carry;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) carry = 0;
-  __syncthreads();
-  for (int base = 0; base < batch; base += 1024) {
-    const int b = base + tid;
+// ------------------------------------------------------------- planning
+// Done by warp 0 of every decode CTA at start (no separate kernel): the total
+// page count U of the batch, the number R of page ranges in use, and for this
+// CTA's range r its first sequence and that sequence's first page.  The
+// leader CTA (0, 0) also validates the lengths and writes the page prefix
+// sums and (U, R) to the workspace for the combine kernel.
+
+struct CtaPlan {
+  int64_t U;
+  int64_t ps_first;  // first page of sequence b_first in the concatenation
+  int32_t R;
+  int32_t b_first;
+};
+
+// Pages of sequence b: 0 for a non-positive length, at most max_pages.
+IRIS_DEV int32_t seq_pages(const DecodeParams& p, int b) {
+  const int32_t L = p.seq_lens[b];
+  if (L <= 0) return 0;
+  const int32_t np = (L + kPage - 1) / kPage;
+  return np < p.max_pages ? np : p.max_pages;
+}
+
+IRIS_DEV void plan_cta(const DecodeParams& p, int r, int ranges, bool leader, int lane, CtaPlan* out) {
+  int64_t U = 0;
+  for (int base = 0; base < p.batch; base += 32) {
+    const int b = base + lane;
     int32_t np = 0;
-    if (b < batch) {
-      const int32_t L = seq_lens[b];
+    if (b < p.batch) {
+      const int32_t L = p.seq_lens[b];
       if (L <= 0) {
-        set_error(err, IRIS_ERR_SEQ_LEN);
+        if (leader) set_error(p.err, IRIS_ERR_SEQ_LEN);
       } else {
         np = (L + kPage - 1) / kPage;
-        if (np > max_pages) {
-          set_error(err, IRIS_ERR_BLOCK_TABLE);
-          np = max_pages;
+        if (np > p.max_pages) {
+          if (leader) set_error(p.err, IRIS_ERR_BLOCK_TABLE);
+          np = p.max_pages;
         }
       }
     }
@@ -125,42 +136,49 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const int32_t* __rest
       const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
       if (lane >= o) x += y;
     }
-    if (lane == 31) warp_tot[warp] = x;
-    __syncthreads();
-    if (warp == 0) {
-      int32_t w = warp_tot[lane];
+    if (leader && b < p.batch) const_cast<int32_t*>(p.prefix)[b] = static_cast<int32_t>(U + x - np);
+    U += __shfl_sync(0xffffffffu, x, 31);
+  }
+  int32_t R = 0;
+  if (U > 0) {
+    const int64_t want = (U + kMinPagesPerRange - 1) / kMinPagesPerRange;
+    R = static_cast<int32_t>(want < ranges ? want : ranges);
+  }
+  if (leader && lane == 0) {
+    const_cast<int32_t*>(p.prefix)[p.batch] = static_cast<int32_t>(U);
+    const_cast<int32_t*>(p.meta)[0] = static_cast<int32_t>(U);
+    const_cast<int32_t*>(p.meta)[1] = R;
+  }
+  int32_t bf = 0;
+  int64_t psf = 0;
+  if (r < R) {
+    // the sequence holding page u0: the first b whose pages end past u0
+    const int64_t u0 = range_start(r, U, R);
+    int64_t carry = 0;
+    for (int base = 0; base < p.batch; base += 32) {
+      const int b = base + lane;
+      const int32_t np = b < p.batch ? seq_pages(p, b) : 0;
+      int32_t x = np;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
-        const int32_t y = __shfl_up_sync(0xffffffffu, w, o);
-        if (lane >= o) w += y;
+        const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
       }
-      warp_tot[lane] = w;  // inclusive over warps
+      const unsigned hit = __ballot_sync(0xffffffffu, b < p.batch && carry + x > u0);
+      if (hit) {
+        const int i = __ffs(hit) - 1;
+        bf = base + i;
+        psf = carry + __shfl_sync(0xffffffffu, x - np, i);
+        break;
+      }
+      carry += __shfl_sync(0xffffffffu, x, 31);
     }
-    __syncthreads();
-    const int32_t excl = carry + (warp ? warp_tot[warp - 1] : 0) + x - np;
-    if (b < batch) prefix[b] = excl;
-    __syncthreads();
-    if (tid == 0) carry += warp_tot[31];
-    __syncthreads();
   }
-  const int32_t U = carry;
-  int32_t reff = 0;
-  if (U > 0) reff = min(ranges, max(1, (U + min_pages - 1) / min_pages));
-  if (tid == 0) {
-    prefix[batch] = U;
-    meta[0] = U;
-    meta[1] = reff;
-  }
-  __syncthreads();
-  for (int r = tid; r < reff; r += 1024) {
-    const int64_t u0 = range_start(r, U, reff);
-    int lo = 0, hi = batch;  // largest b with prefix[b] <= u0 (prefix[batch] = U > u0)
-    while (hi - lo > 1) {
-      const int mid = (lo + hi) >> 1;
-      if (prefix[mid] <= u0) lo = mid;
-      else hi = mid;
-    }
-    range_seq[r] = lo;
+  if (lane == 0) {
+    out->U = U;
+    out->R = R;
+    out->b_first = bf;
+    out->ps_first = psf;
   }
 }
 
@@ -485,8 +503,8 @@ IRIS_DEV void finish_piece(const DecodeParams& p, WarpState<D, NT>& st, int b, i
 template <int D>
 IRIS_DEV void run_producer(const CUtensorMap* kmap_p, const CUtensorMap* vmap_p, const DecodeParams& p,
                            uint8_t* smem, int stage_bytes, int S, int HB, int hblk, int64_t u0, int64_t u1,
-                           int b_first, uint64_t* full, uint32_t full_u32, uint32_t empty_u32, int scale_block,
-                           int lane) {
+                           int b_first, int64_t ps_first, uint64_t* full, uint32_t full_u32, uint32_t empty_u32,
+                           int scale_block, int lane) {
   using C = DecCfg<D>;
   // All lanes fetch (and validate) page ids 32 at a time, one chunk ahead
   // of lane 0, which waits for free stages and issues the copies.
@@ -500,6 +518,7 @@ IRIS_DEV void run_producer(const CUtensorMap* kmap_p, const CUtensorMap* vmap_p,
   uint32_t ph = 0;    // its ring pass parity
   bool alive = true;
   int b = b_first;
+  int64_t ps = ps_first;  // first page of sequence b
   int64_t u = u0;
   auto fetch_ids = [&](const int32_t* row, int64_t first, int64_t count) -> int32_t {
     int32_t pid = 0;
@@ -513,8 +532,12 @@ IRIS_DEV void run_producer(const CUtensorMap* kmap_p, const CUtensorMap* vmap_p,
     return pid;
   };
   while (alive && u < u1) {
-    const int64_t ps = p.prefix[b], pe = p.prefix[b + 1];
-    if (pe <= u) { ++b; continue; }
+    const int64_t pe = ps + seq_pages(p, b);
+    if (pe <= u) {
+      ps = pe;
+      ++b;
+      continue;
+    }
     const int64_t hi = pe < u1 ? pe : u1;
     const int32_t* bt_row = p.block_table + static_cast<int64_t>(b) * p.bt_stride;
     int64_t chunk = u;
@@ -547,6 +570,7 @@ IRIS_DEV void run_producer(const CUtensorMap* kmap_p, const CUtensorMap* vmap_p,
       chunk = next;
     }
     u = hi;
+    ps = pe;
     ++b;
   }
   // drain: every copy this CTA issued has landed before it exits
@@ -570,8 +594,7 @@ __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ CUtensorM
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int HB = p.hb;
   const int S = p.stages;
-  const int U = p.meta[0], R = p.meta[1];
-  if (r >= R) return;  // uniform per CTA
+  __shared__ CtaPlan plan;
 
   const int scale_block = kPage * p.hkv * C::kGroups * 2;  // bytes of one page's K (or V) scales
   const int stage_bytes = ((2 * HB * C::kTileBytes + 2 * scale_block) + 1023) & ~1023;
@@ -585,15 +608,20 @@ __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ CUtensorM
     }
     fence_barrier_init();
   }
+  if (warp == 0) plan_cta(p, r, gridDim.y, blockIdx.x == 0 && r == 0, lane, &plan);
   __syncthreads();
+  const int64_t U = plan.U;
+  const int R = plan.R;
+  if (r >= R) return;  // uniform per CTA (nothing was issued yet)
 
   const int64_t u0 = range_start(r, U, R), u1 = range_start(r + 1, U, R);
-  const int b_first = p.range_seq[r];
+  const int b_first = plan.b_first;
+  const int64_t ps_first = plan.ps_first;
   const uint32_t full_u32 = smem_u32(full), empty_u32 = smem_u32(empty);
 
   if (warp == HB) {
-    run_producer<D>(&kmap, &vmap, p, smem, stage_bytes, S, HB, hblk, u0, u1, b_first, full, full_u32, empty_u32,
-                    scale_block, lane);
+    run_producer<D>(&kmap, &vmap, p, smem, stage_bytes, S, HB, hblk, u0, u1, b_first, ps_first, full, full_u32,
+                    empty_u32, scale_block, lane);
     return;
   }
 
@@ -610,10 +638,15 @@ __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ CUtensorM
   uint32_t ph = 0;
   uint32_t stage = ring;  // base address of stage s
   int b = b_first;
+  int64_t ps = ps_first;  // first page of sequence b
   int64_t u = u0;
   while (u < u1) {
-    const int64_t ps = p.prefix[b], pe = p.prefix[b + 1];
-    if (pe <= u) { ++b; continue; }
+    const int64_t pe = ps + seq_pages(p, b);
+    if (pe <= u) {
+      ps = pe;
+      ++b;
+      continue;
+    }
     const int64_t hi = pe < u1 ? pe : u1;
     const int L = min(p.seq_lens[b], p.max_pages * kPage);
     load_query<D, NT>(st, p.query + (static_cast<int64_t>(b) * p.hq + kvh * p.qpk) * D, p.qpk, lane);
@@ -674,6 +707,7 @@ __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ CUtensorM
     const int64_t rec = static_cast<int64_t>(r) * 2 + (u == u0 ? 0 : 1);
     finish_piece<D, NT>(p, st, b, kvh, complete, rec, lane);
     u = hi;
+    ps = pe;
     ++b;
   }
 }
@@ -1011,8 +1045,7 @@ __global__ void __maxnreg__(128) decode_pair_kernel(const __grid_constant__ CUte
   const int HB = p.hb;
   const int NW = HB / HP;  // consumer warps
   const int S = p.stages;
-  const int U = p.meta[0], R = p.meta[1];
-  if (r >= R) return;  // uniform per CTA
+  __shared__ CtaPlan plan;
 
   const int scale_block = kPage * p.hkv * C::kGroups * 2;
   const int stage_bytes = ((2 * HB * C::kTileBytes + 2 * scale_block) + 1023) & ~1023;
@@ -1029,15 +1062,20 @@ __global__ void __maxnreg__(128) decode_pair_kernel(const __grid_constant__ CUte
     fence_barrier_init();
   }
   if (threadIdx.x < 64) reinterpret_cast<uint32_t*>(zero_blk)[threadIdx.x] = 0u;
+  if (warp == 0) plan_cta(p, r, gridDim.y, blockIdx.x == 0 && r == 0, lane, &plan);
   __syncthreads();
+  const int64_t U = plan.U;
+  const int R = plan.R;
+  if (r >= R) return;  // uniform per CTA (nothing was issued yet)
 
   const int64_t u0 = range_start(r, U, R), u1 = range_start(r + 1, U, R);
-  const int b_first = p.range_seq[r];
+  const int b_first = plan.b_first;
+  const int64_t ps_first = plan.ps_first;
   const uint32_t full_u32 = smem_u32(full), empty_u32 = smem_u32(empty);
 
   if (warp == NW) {
-    run_producer<D>(&kmap, &vmap, p, smem, stage_bytes, S, HB, hblk, u0, u1, b_first, full, full_u32, empty_u32,
-                    scale_block, lane);
+    run_producer<D>(&kmap, &vmap, p, smem, stage_bytes, S, HB, hblk, u0, u1, b_first, ps_first, full, full_u32,
+                    empty_u32, scale_block, lane);
     return;
   }
 
@@ -1064,10 +1102,15 @@ __global__ void __maxnreg__(128) decode_pair_kernel(const __grid_constant__ CUte
   uint32_t ph = 0;
   uint32_t stage = ring;
   int b = b_first;
+  int64_t ps = ps_first;  // first page of sequence b
   int64_t u = u0;
   while (u < u1) {
-    const int64_t ps = p.prefix[b], pe = p.prefix[b + 1];
-    if (pe <= u) { ++b; continue; }
+    const int64_t pe = ps + seq_pages(p, b);
+    if (pe <= u) {
+      ps = pe;
+      ++b;
+      continue;
+    }
     const int64_t hi = pe < u1 ? pe : u1;
     const int L = min(p.seq_lens[b], p.max_pages * kPage);
     __syncwarp();  // the previous piece's ldmatrix reads of the tile are done
@@ -1098,6 +1141,7 @@ __global__ void __maxnreg__(128) decode_pair_kernel(const __grid_constant__ CUte
     const int64_t rec = static_cast<int64_t>(r) * 2 + (u == u0 ? 0 : 1);
     pair_finish_piece<D, HP>(p, st, b, kv0, complete, rec, lane);
     u = hi;
+    ps = pe;
     ++b;
   }
 }
@@ -1178,7 +1222,6 @@ using namespace iris;
 
 namespace {
 
-constexpr int kMinPagesPerRange = 4;
 constexpr int kSmemBudgetPerSm = 200 * 1024;
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -1382,7 +1425,6 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct Workspace {
   int32_t* prefix;
-  int32_t* range_seq;
   int32_t* meta;
   float* rec_lse;
   float* rec_o;
@@ -1395,8 +1437,6 @@ Workspace carve(void* base, int batch, int hq, int D, int ranges) {
   size_t off = 0;
   w.prefix = reinterpret_cast<int32_t*>(p + off);
   off += align256(sizeof(int32_t) * (batch + 1));
-  w.range_seq = reinterpret_cast<int32_t*>(p + off);
-  off += align256(sizeof(int32_t) * ranges);
   w.meta = reinterpret_cast<int32_t*>(p + off);
   off += 256;
   w.rec_lse = reinterpret_cast<float*>(p + off);
@@ -1415,14 +1455,6 @@ cudaError_t launch_decode(const Plan& pl, const CUtensorMap& km, const CUtensorM
   p.stages = ls.stages;
   const int32_t ranges = ls.ranges < ranges_cap ? ls.ranges : ranges_cap;
   cudaError_t e;
-  decode_plan_kernel<<<1, 1024, 0, stream>>>(p.seq_lens, p.batch, p.max_pages, ranges, kMinPagesPerRange,
-                                             const_cast<int32_t*>(p.prefix), const_cast<int32_t*>(p.range_seq),
-                                             const_cast<int32_t*>(p.meta), p.err);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) {
-    record_cuda_error(e, "decode_plan_kernel launch");
-    return e;
-  }
   e = ensure_smem_attr(pl.fn, device, ls.smem);  // no-op once raised
   if (e != cudaSuccess) {
     record_cuda_error(e, "cudaFuncSetAttribute(max dynamic smem)");
@@ -1514,7 +1546,6 @@ extern "C" int iris_b200_int4_paged_decode(const void* query, const void* k_data
   p.rec_o = ws.rec_o;
   p.rec_lse = ws.rec_lse;
   p.prefix = ws.prefix;
-  p.range_seq = ws.range_seq;
   p.meta = ws.meta;
   p.err = error_word;
   p.num_pages = num_pages;
