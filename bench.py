@@ -58,6 +58,101 @@ PF_S, PF_L = 8, 8192
 PF_BYTES = PF_S * PF_L * HKV * (4 * D + D + D // 8) + PF_S * PF_L * 8 + PF_L * 2 * (D // 2) * 2
 
 
+# BASELINE config 4 (70B-shaped long context): 16 sequences x 131,072 tokens,
+# Hq 64, Hkv 8, D 128; split-context over the ranks in 8192-token splits,
+# every rank's cache holding only its splits; one NCCL all-gather + merge.
+C4_B, C4_L, C4_HQ, C4_HKV, C4_SPLIT = 16, 131072, 64, 8, 8192
+C4_BYTES = C4_B * C4_L * C4_HKV * (D + D // 8) + 2 * C4_B * C4_HQ * D * 2 + C4_B * (C4_L // P) * 4 + C4_B * 4
+# BASELINE config 3 (MHA, D 64, varlen): 128 sequences, Hq = Hkv = 16,
+# L ~ U[1, 16384] (seed 1); sequences sharded over the ranks by token count.
+C3_B, C3_H, C3_D, C3_LMAX = 128, 16, 64, 16384
+
+
+def _fill_cache(dev, g, kd, vd, ks, vs, slots, positions, hkv, d, cos, sin, chunk=65536):
+    """Write synthetic K/V ~ N(0, 0.5) through the fused append, in chunks."""
+    from iris_kernel.fused_kv import fused_rope_int4_paged_append
+
+    for t0 in range(0, slots.numel(), chunk):
+        t1 = min(slots.numel(), t0 + chunk)
+        k = (torch.randn(t1 - t0, hkv, d, generator=g, device=dev) * 0.5).half()
+        v = (torch.randn(t1 - t0, hkv, d, generator=g, device=dev) * 0.5).half()
+        fused_rope_int4_paged_append(k, v, positions[t0:t1].contiguous(), slots[t0:t1].contiguous(), cos, sin,
+                                     kd, vd, ks, vs, rotary_dim=d, page_size=P)
+
+
+def build_c4(dev, rank, world, seed):
+    """This rank's share of config 4: only the pages of its splits exist in
+    its cache; the block table maps its split columns to them."""
+    from iris_kernel import parallel
+    from oracle import iris_oracle as orc  # RoPE table builder only (host arrays)
+
+    plan = parallel.plan_split_context([C4_L] * C4_B, world, rank, split_tokens=C4_SPLIT)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    n_local = int(sum(-(-int(x) // P) for x in plan.lens))
+    perm = torch.randperm(n_local, generator=g, device=dev).int()
+    bt = torch.zeros(C4_B, C4_L // P, dtype=torch.int32, device=dev)
+    cols = torch.from_numpy(plan.cols).to(dev)
+    npg = torch.from_numpy((plan.lens + P - 1) // P).to(dev)
+    off = 0
+    slot_l, pos_l = [], []
+    for i, b in enumerate(plan.seqs.tolist()):
+        n = int(npg[i])
+        pages = perm[off:off + n]
+        bt[b, cols[i, :n]] = pages
+        tok = (cols[i, :n].int()[:, None] * P + torch.arange(P, device=dev, dtype=torch.int32)).reshape(-1)
+        slot_l.append((pages[:, None] * P + torch.arange(P, device=dev, dtype=torch.int32)).reshape(-1))
+        pos_l.append(tok)
+        off += n
+    kd = torch.zeros(n_local, P, C4_HKV, D // 2, dtype=torch.uint8, device=dev)
+    vd = torch.zeros_like(kd)
+    ks = torch.zeros(n_local, P, C4_HKV, D // G, dtype=torch.float16, device=dev)
+    vs = torch.zeros_like(ks)
+    cos_np, sin_np = orc.rope_cache(C4_L, D, 500000.0)
+    cos, sin = torch.from_numpy(cos_np).to(dev), torch.from_numpy(sin_np).to(dev)
+    _fill_cache(dev, g, kd, vd, ks, vs, torch.cat(slot_l), torch.cat(pos_l), C4_HKV, D, cos, sin)
+    q = torch.randn(C4_B, C4_HQ, D, generator=torch.Generator(device=dev).manual_seed(4), device=dev).half()
+    return dict(plan=plan, q=q, kd=kd, vd=vd, ks=ks, vs=vs, bt=bt)
+
+
+def build_c3(dev, rank, world, seed):
+    """This rank's shard of config 3 (whole sequences, balanced by tokens)."""
+    from iris_kernel import parallel
+    from oracle import iris_oracle as orc  # RoPE table builder only (host arrays)
+
+    lens_all = np.random.default_rng(1).integers(1, C3_LMAX + 1, size=C3_B)
+    mine = parallel.balance_sequences(lens_all, world)[rank]
+    lens = lens_all[mine]
+    g = torch.Generator(device=dev).manual_seed(seed)
+    npg = (lens + P - 1) // P
+    pool = int(npg.sum())
+    perm = torch.randperm(pool, generator=g, device=dev).int()
+    width = int(npg.max())
+    bt = torch.zeros(len(mine), width, dtype=torch.int32, device=dev)
+    off = 0
+    slot_l, pos_l = [], []
+    for i, L_ in enumerate(lens.tolist()):
+        n = int(npg[i])
+        pages = perm[off:off + n]
+        bt[i, :n] = pages
+        slot_l.append((pages[:, None] * P + torch.arange(P, device=dev, dtype=torch.int32)).reshape(-1)[:L_])
+        pos_l.append(torch.arange(L_, device=dev, dtype=torch.int32))
+        off += n
+    kd = torch.zeros(pool, P, C3_H, C3_D // 2, dtype=torch.uint8, device=dev)
+    vd = torch.zeros_like(kd)
+    ks = torch.zeros(pool, P, C3_H, C3_D // G, dtype=torch.float16, device=dev)
+    vs = torch.zeros_like(ks)
+    cos_np, sin_np = orc.rope_cache(C3_LMAX, C3_D)
+    cos, sin = torch.from_numpy(cos_np).to(dev), torch.from_numpy(sin_np).to(dev)
+    _fill_cache(dev, g, kd, vd, ks, vs, torch.cat(slot_l), torch.cat(pos_l), C3_H, C3_D, cos, sin)
+    q = torch.randn(len(mine), C3_H, C3_D, generator=g, device=dev).half()
+    nbytes = int(lens.sum()) * C3_H * (C3_D + C3_D // 8) + 2 * len(mine) * C3_H * C3_D * 2 + int(npg.sum()) * 4
+    total = int(lens_all.sum()) * C3_H * (C3_D + C3_D // 8) + 2 * C3_B * C3_H * C3_D * 2 + int(
+        ((lens_all + P - 1) // P).sum()) * 4
+    return dict(q=q, kd=kd, vd=vd, ks=ks, vs=vs, bt=bt,
+                lens=torch.from_numpy(lens.astype(np.int32)).to(dev),
+                out=torch.empty_like(q), bytes=nbytes, total_bytes=total)
+
+
 def _peak_gbs():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -379,6 +474,29 @@ def main():
     del g_pf, x
     ms_pf = max_over_ranks(ms_pf, dist, dev)
     pf_us = ms_pf / pf_steps * 1e3
+
+    # config 4: split-context decode over the ranks (one NCCL all-gather per step)
+    from iris_kernel import parallel
+
+    c4 = build_c4(dev, rank, world, seed=44 + rank)
+    dec4 = parallel.SplitContextDecoder(c4["plan"], c4["bt"], C4_HQ, D)
+    iris_kernel.set_validation_mode("deferred")
+    g_c4 = graph_of(lambda: dec4(c4["q"], c4["kd"], c4["vd"], c4["ks"], c4["vs"]), dev)
+    x_steps = max(10, min(args.steps, 100))
+    ms_c4 = timed(g_c4.replay, x_steps, dev, dist, args.warmup)
+    iris_kernel.check_errors(dev)
+    del g_c4, dec4, c4  # the graph holds an NCCL call: released before the process group
+    # config 3: sequence-sharded MHA decode, no collective
+    c3 = build_c3(dev, rank, world, seed=33 + rank)
+    g_c3 = graph_of(lambda: fused_int4_paged_decode_attention(c3["q"], c3["kd"], c3["vd"], c3["ks"], c3["vs"],
+                                                              c3["bt"], c3["lens"], c3["out"]), dev)
+    ms_c3 = timed(g_c3.replay, x_steps, dev, dist, args.warmup)
+    iris_kernel.check_errors(dev)
+    iris_kernel.set_validation_mode("sync")
+    c3_total = c3["total_bytes"]
+    del g_c3, c3
+    c4_us = max_over_ranks(ms_c4, dist, dev) / x_steps * 1e3
+    c3_us = max_over_ranks(ms_c3, dist, dev) / x_steps * 1e3
     ms = max_over_ranks(ms, dist, dev)
     ms_dec = max_over_ranks(ms_dec, dist, dev)
     ms_app = max_over_ranks(ms_app, dist, dev)
@@ -450,13 +568,23 @@ def main():
                                "us": pf_us, "tbs": world * PF_BYTES / (pf_us * 1e-6) / 1e12,
                                "pct_of_measured": 100 * PF_BYTES / (pf_us * 1e-6) / 1e9 / _peak_gbs()[0],
                                "tokens_per_s": world * PF_S * PF_L / (pf_us * 1e-6), "bytes": PF_BYTES},
+            "config4_split_context": {
+                "config": "BASELINE config 4: 16 x 131072 tokens, Hq 64, Hkv 8, D 128, 8192-token splits dealt "
+                          "over the ranks; each rank's cache holds only its splits",
+                "us": c4_us, "tbs": C4_BYTES / (c4_us * 1e-6) / 1e12, "bytes": C4_BYTES,
+                "collective": "one NCCL all_gather_into_tensor of packed (O, lse) fp32 per step" if world > 1
+                              else "none (one GPU)"},
+            "config3_sharded": {
+                "config": "BASELINE config 3: 128 sequences, L ~ U[1,16384] (seed 1), Hq = Hkv = 16, D 64; "
+                          "whole sequences sharded over the ranks by token count, no collective",
+                "us": c3_us, "tbs": c3_total / (c3_us * 1e-6) / 1e12, "bytes": c3_total},
             "step_bytes": STEP_BYTES, "decode_bytes": DECODE_BYTES, "append_bytes": APPEND_BYTES,
             "e2e": {"value": e2e_value, "unit": "TB/s", "ms_per_step": ms_e2e / args.steps,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": 5 * args.steps,
+            "gpu_launches": 4 * args.steps,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "traffic": traffic,
-                         "kernel": "decode (plan + decode + combine launches) timed alone from a CUDA graph"},
+                         "kernel": "decode (decode + combine launches) timed alone from a CUDA graph"},
             "cpu_baseline": cpu,
             "clocks": clocks,
         }

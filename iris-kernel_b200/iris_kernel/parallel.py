@@ -155,6 +155,63 @@ def pack_partials(o_local: torch.Tensor, lse_local: torch.Tensor, seqs, batch: i
     return buf
 
 
+class SplitContextDecoder:
+    """Split-context decode for one GPU's plan, with everything that does not
+    change between steps (the local block table, the token counts, the
+    all-gather buffers) prepared once, so a step is three kernels and one
+    all-gather that a CUDA graph can capture.
+
+    ``block_table`` maps this GPU's splits to pages of its own cache; entries
+    of other GPUs' splits are not read."""
+
+    def __init__(self, plan: SplitPlan, block_table: torch.Tensor, num_q_heads: int, head_dim: int, *, group=None,
+                 page_size: int = 16, group_size: int = 32, softmax_scale=None):
+        import torch.distributed as dist
+
+        self.plan, self.group = plan, group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        if plan.world != self.world:
+            raise ValueError("plan does not match the process group")
+        dev = block_table.device
+        self.hq, self.d = num_q_heads, head_dim
+        self.kw = dict(page_size=page_size, group_size=group_size, softmax_scale=softmax_scale)
+        self.local_bt = local_block_table(plan, block_table)
+        self.lens = torch.from_numpy(plan.lens.astype(np.int32)).to(dev)
+        self.idx = torch.from_numpy(plan.seqs).to(dev)
+        n = packed_size(plan.batch, num_q_heads, head_dim)
+        self.send = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.recv = torch.empty(self.world * n, dtype=torch.float32, device=dev)
+        self.output = torch.empty((plan.batch, num_q_heads, head_dim), dtype=torch.float16, device=dev)
+        o, lse = packed_views(self.send, plan.batch, num_q_heads, head_dim)
+        lse.fill_(float("-inf"))  # sequences without local tokens keep lse = -inf
+        self._o, self._lse = o, lse
+        m = len(plan.seqs)
+        self._o_l = torch.empty((m, num_q_heads, head_dim), dtype=torch.float32, device=dev)
+        self._lse_l = torch.empty((m, num_q_heads), dtype=torch.float32, device=dev)
+
+    def __call__(self, query, k_data, v_data, k_scale, v_scale) -> torch.Tensor:
+        import torch.distributed as dist
+
+        plan = self.plan
+        if query.shape != (plan.batch, self.hq, self.d):
+            raise ValueError("query does not match the plan")
+        if len(plan.seqs):
+            if plan.covers_every_sequence:
+                decode_partial(query, k_data, v_data, k_scale, v_scale, self.local_bt, self.lens, out=self._o,
+                               lse=self._lse, **self.kw)
+            else:
+                decode_partial(query.index_select(0, self.idx), k_data, v_data, k_scale, v_scale, self.local_bt,
+                               self.lens, out=self._o_l, lse=self._lse_l, **self.kw)
+                self._o.index_copy_(0, self.idx, self._o_l)
+                self._lse.index_copy_(0, self.idx, self._lse_l)
+        if self.world > 1:
+            dist.all_gather_into_tensor(self.recv, self.send, group=self.group)
+            parts = self.recv
+        else:
+            parts = self.send
+        return merge_lse_packed(parts, self.world, plan.batch, self.hq, self.d, self.output)
+
+
 def split_context_decode(query, k_data, v_data, k_scale, v_scale, block_table, plan: SplitPlan, *,
                          group=None, page_size: int = 16, group_size: int = 32, softmax_scale=None,
                          output: torch.Tensor | None = None) -> torch.Tensor:

@@ -104,6 +104,36 @@ def test_sequence_sharding_reassembles_to_oracle():
     assert_decode_close(out, orc.decode_attention(*[c[k] for k in cases.DECODE_KEYS]))
 
 
+def test_split_context_decoder_replays_in_a_cuda_graph():
+    """The prepared one-GPU decoder (world of one: no collective) captured in a
+    CUDA graph and replayed gives the oracle's output."""
+    import iris_kernel
+    from iris_kernel import parallel as P
+
+    c = _case()
+    t = to_dev(c, cases.DECODE_KEYS)
+    plan = P.plan_split_context(c["seq_lens"], 1, 0, split_tokens=256)
+    dec = P.SplitContextDecoder(plan, t["block_table"], 32, 128)
+    args = [t[k] for k in ("query", "k_data", "v_data", "k_scale", "v_scale")]
+    iris_kernel.set_validation_mode("deferred")
+    try:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            dec(*args)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            out = dec(*args)
+        dec.output.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        iris_kernel.check_errors()
+    finally:
+        iris_kernel.set_validation_mode("sync")
+    assert_decode_close(out, orc.decode_attention(*[c[k] for k in cases.DECODE_KEYS]))
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -133,6 +163,10 @@ def _nccl_worker(rank, world, port, c, expected):
                                      t["block_table"], plan)
         torch.cuda.synchronize()
         assert_decode_close(out, expected)
+        dec = P.SplitContextDecoder(plan, t["block_table"], t["query"].shape[1], t["query"].shape[2])
+        out2 = dec(t["query"], t["k_data"], t["v_data"], t["k_scale"], t["v_scale"])
+        torch.cuda.synchronize()
+        assert torch.equal(out2, out)
     finally:
         dist.destroy_process_group()
 
