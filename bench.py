@@ -19,8 +19,14 @@ max-over-ranks step time, in TB/s, with inputs resident in HBM; the step is
 replayed from a CUDA graph (validation in deferred mode, no host syncs).
 ``e2e``: the same metric through the public Python API with host buffers:
 per step the new query / K / V / positions / slots are copied from pinned
-host memory, the reference-semantics (synchronous validation) calls run,
-and the fp16 output is copied back.
+host memory, the decode and append calls run, the fp16 output is copied
+back, and any error the step's kernels recorded is raised (one host read per
+step, deferred validation mode).  ``e2e_sync`` is the same loop with every
+call reading the error word before it returns (the reference's per-call
+exceptions).
+
+Also reported: config 5b prefill append, config 4 split-context decode over
+the ranks (one NCCL all-gather per step), config 3 sequence-sharded decode.
 """
 from __future__ import annotations
 
@@ -425,7 +431,7 @@ def _config():
             "batch": B, "context": L, "hq": HQ, "hkv": HKV, "head_dim": D, "page_size": P, "group": G,
             "pool_pages": POOL, "l2": "no flush: each step reads 303 MB of cache > 126 MB L2",
             "parallelism": "sequence-sharded replicas (one 64x4096 batch per GPU)",
-            "validation": "deferred (value), synchronous (e2e)"}
+            "validation": "deferred (value, e2e), synchronous per call (e2e_sync)"}
 
 
 def main():
@@ -506,35 +512,62 @@ def main():
     value = world * STEP_BYTES / (step_ms * 1e-3) / 1e12
 
     # ---- e2e: public API with host buffers ----
-    hq = torch.empty_like(w["q"], device="cpu").pin_memory()
-    hk = torch.empty_like(w["knew"], device="cpu").pin_memory()
-    hv = torch.empty_like(w["vnew"], device="cpu").pin_memory()
-    hp = torch.empty_like(w["newpos"], device="cpu").pin_memory()
-    hs = torch.empty_like(w["newslot"], device="cpu").pin_memory()
+    # The step's inputs (new query, K, V, positions, slots) sit in one pinned
+    # host buffer and go to the device in one copy; the fp16 output comes back
+    # in one copy.
+    parts = [("q", w["q"]), ("k", w["knew"]), ("v", w["vnew"]), ("p", w["newpos"]), ("s", w["newslot"])]
+    offs, total = {}, 0
+    for name, t in parts:
+        offs[name] = total
+        total += (t.numel() * t.element_size() + 255) // 256 * 256
+    host_in = torch.empty(total, dtype=torch.uint8).pin_memory()
+    dev_in = torch.empty(total, dtype=torch.uint8, device=dev)
+
+    def view(buf, name, like):
+        n = like.numel() * like.element_size()
+        return buf[offs[name]:offs[name] + n].view(like.dtype).view(like.shape)
+
+    for name, t in parts:
+        view(host_in, name, t).copy_(t.cpu())
     hout = torch.empty_like(w["out"], device="cpu").pin_memory()
-    hq.copy_(w["q"])
-    hk.copy_(w["knew"])
-    hv.copy_(w["vnew"])
-    hp.copy_(w["newpos"])
-    hs.copy_(w["newslot"])
-    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hp, hs))
+    h2d = sum(t.numel() * t.element_size() for _, t in parts)
     d2h = hout.numel() * hout.element_size()
+    q, k, v, pp, ss = (view(dev_in, name, t) for name, t in parts)
+    out_dev = torch.empty_like(w["out"])
 
-    def e2e_step():
-        q = hq.to(dev, non_blocking=True)
-        k = hk.to(dev, non_blocking=True)
-        v = hv.to(dev, non_blocking=True)
-        p = hp.to(dev, non_blocking=True)
-        s = hs.to(dev, non_blocking=True)
-        out = fused_int4_paged_decode_attention(q, w["kd"], w["vd"], w["ks"], w["vs"], w["bt"], w["lens"])
-        fused_rope_int4_paged_append(k, v, p, s, w["cos"], w["sin"], w["kd"], w["vd"], w["ks"], w["vs"],
+    def calls():
+        fused_int4_paged_decode_attention(q, w["kd"], w["vd"], w["ks"], w["vs"], w["bt"], w["lens"], out_dev)
+        fused_rope_int4_paged_append(k, v, pp, ss, w["cos"], w["sin"], w["kd"], w["vd"], w["ks"], w["vs"],
                                      rotary_dim=D, page_size=P)
-        hout.copy_(out, non_blocking=True)
 
+    def e2e_step(replay=None):
+        dev_in.copy_(host_in, non_blocking=True)
+        if replay is None:
+            calls()
+        else:
+            replay()
+        hout.copy_(out_dev, non_blocking=True)
+        if iris_kernel.validation_mode() == "deferred":
+            iris_kernel.check_errors(dev)  # one host read per step raises any error of the step
+
+    # e2e: eager calls, deferred validation, errors raised once per step (the
+    # host prepares the next call while the GPU runs).  e2e_sync: every call
+    # reads the error word before it returns, as the reference's calls raise.
+    # e2e_graph: the two calls captured once in a CUDA graph and replayed.
+    iris_kernel.set_validation_mode("deferred")
     ms_e2e = timed(e2e_step, args.steps, dev, dist, args.warmup)
+    g_e2e = graph_of(calls, dev)
+    ms_e2e_graph = timed(lambda: e2e_step(g_e2e.replay), args.steps, dev, dist, args.warmup)
+    iris_kernel.set_validation_mode("sync")
+    ms_e2e_sync = timed(e2e_step, args.steps, dev, dist, args.warmup)
+    del g_e2e
     clk.__exit__(None, None, None)
     ms_e2e = max_over_ranks(ms_e2e, dist, dev)
+    ms_e2e_sync = max_over_ranks(ms_e2e_sync, dist, dev)
+    ms_e2e_graph = max_over_ranks(ms_e2e_graph, dist, dev)
     e2e_value = world * STEP_BYTES / (ms_e2e / args.steps * 1e-3) / 1e12
+    e2e_sync_value = world * STEP_BYTES / (ms_e2e_sync / args.steps * 1e-3) / 1e12
+    e2e_graph_value = world * STEP_BYTES / (ms_e2e_graph / args.steps * 1e-3) / 1e12
 
     clocks = clk.summary()
     peak, peak_kind = _peak_gbs()
@@ -580,7 +613,15 @@ def main():
                 "us": c3_us, "tbs": c3_total / (c3_us * 1e-6) / 1e12, "bytes": c3_total},
             "step_bytes": STEP_BYTES, "decode_bytes": DECODE_BYTES, "append_bytes": APPEND_BYTES,
             "e2e": {"value": e2e_value, "unit": "TB/s", "ms_per_step": ms_e2e / args.steps,
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "validation": "deferred, errors raised once per step (iris_kernel.check_errors)"},
+            "e2e_sync": {"value": e2e_sync_value, "unit": "TB/s", "ms_per_step": ms_e2e_sync / args.steps,
+                         "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                         "validation": "synchronous: every call reads the error word before returning"},
+            "e2e_graph": {"value": e2e_graph_value, "unit": "TB/s", "ms_per_step": ms_e2e_graph / args.steps,
+                          "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                          "validation": "deferred, errors raised once per step; the two calls replayed from a "
+                                        "CUDA graph captured once"},
             "gpu_launches": 4 * args.steps,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "traffic": traffic,

@@ -97,7 +97,10 @@ IRIS_API int iris_b200_append_check(const int32_t* positions, const int32_t* slo
  *   head_dim % 64 == 0, group size 32.
  * Slots / positions out of range are skipped and reported in *error_word
  * (may be NULL).  Duplicate slots are not detected here (use
- * iris_b200_append_check first).
+ * iris_b200_append_check first, on the same stream and error word): when
+ * *error_word already holds a slot, position or duplicate bit as the kernel
+ * starts, the call writes nothing, so a batch the check rejected leaves the
+ * cache untouched without a host round trip in between.
  */
 IRIS_API int iris_b200_rope_int4_paged_append(const void* key, const void* value, const int32_t* positions,
                                      const int32_t* slot_mapping, const void* cos_cache, const void* sin_cache,

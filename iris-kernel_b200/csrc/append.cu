@@ -187,6 +187,8 @@ struct AppendCfg {
   static constexpr int kThreads = kRows * kTpr;
 };
 
+constexpr int32_t kRejectBits = IRIS_ERR_SLOT_RANGE | IRIS_ERR_POS_NEGATIVE | IRIS_ERR_POS_RANGE | IRIS_ERR_DUP_SLOT;
+
 template <int D>
 __global__ void __launch_bounds__(AppendCfg<D>::kThreads) rope_int4_append_kernel(const AppendParams p) {
   using C = AppendCfg<D>;
@@ -198,6 +200,10 @@ __global__ void __launch_bounds__(AppendCfg<D>::kThreads) rope_int4_append_kerne
   const uint32_t tok = p.heads_div.div(row);
   const uint32_t h = row - tok * static_cast<uint32_t>(p.num_heads);
 
+  // A slot / position / duplicate error already recorded (by the check
+  // kernel that runs first) means the batch is rejected: write nothing, as
+  // the reference raises before it writes.
+  if (p.err != nullptr && (*p.err & kRejectBits) != 0) return;
   const int32_t slot = __ldg(p.slots + tok);
   if (slot < 0) return;
   const int32_t pos = __ldg(p.positions + tok);

@@ -1262,6 +1262,39 @@ bool make_kv_map(CUtensorMap* map, const void* base, int D, int hkv, int hb, int
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Tensor maps are pure functions of (base, D, Hkv, head block, pages); the
+// last few are kept so that a decode loop over the same cache does not
+// re-encode them on every call.
+bool cached_kv_map(CUtensorMap* map, const void* base, int D, int hkv, int hb, int64_t num_pages) {
+  struct Entry {
+    const void* base;
+    int D, hkv, hb;
+    int64_t pages;
+    CUtensorMap map;
+  };
+  constexpr int kEntries = 16;
+  static Entry cache[kEntries];
+  static int used = 0, next = 0;
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < used; ++i) {
+      const Entry& e = cache[i];
+      if (e.base == base && e.D == D && e.hkv == hkv && e.hb == hb && e.pages == num_pages) {
+        *map = e.map;
+        return true;
+      }
+    }
+  }
+  if (!make_kv_map(map, base, D, hkv, hb, num_pages)) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  Entry& e = cache[next];
+  e = Entry{base, D, hkv, hb, num_pages, *map};
+  next = (next + 1) % kEntries;
+  if (used < kEntries) ++used;
+  return true;
+}
+
 using DecodeKernelFn = void (*)(CUtensorMap, CUtensorMap, DecodeParams);
 
 // KV heads per consumer warp: groups of at most 4 query heads share a warp's
@@ -1527,8 +1560,8 @@ extern "C" int iris_b200_int4_paged_decode(const void* query, const void* k_data
 
   CUtensorMap km, vm;
   const Plan plan = make_plan(head_dim, qpk, num_kv_heads);
-  if (!make_kv_map(&km, k_data, head_dim, num_kv_heads, plan.hb, num_pages) ||
-      !make_kv_map(&vm, v_data, head_dim, num_kv_heads, plan.hb, num_pages)) {
+  if (!cached_kv_map(&km, k_data, head_dim, num_kv_heads, plan.hb, num_pages) ||
+      !cached_kv_map(&vm, v_data, head_dim, num_kv_heads, plan.hb, num_pages)) {
     snprintf(iris::g_last_error, sizeof(iris::g_last_error), "cuTensorMapEncodeTiled failed (D=%d Hkv=%d pages=%lld)", head_dim,
              num_kv_heads, static_cast<long long>(num_pages));
     return IRIS_ECUDA;

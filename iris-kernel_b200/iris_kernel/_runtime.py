@@ -7,11 +7,16 @@ sequence in fused_attention.py:415-429).  Here the kernels check the data on
 the device and OR ``IRIS_ERR_*`` bits into an int32 error word:
 
 * ``"sync"`` (default): after launching, the wrapper reads the word once and
-  raises the reference's exception type.  The append validates before it
-  writes (the cache is untouched on error, as in the reference); the decode
+  raises the reference's exception type.  The append's check kernel runs
+  before the append kernel, which writes nothing when the check recorded an
+  error (the cache is untouched on error, as in the reference); the decode
   kernels skip bad pages while running and the wrapper raises afterwards.
 * ``"deferred"``: no host synchronisation at all (CUDA-graph friendly); call
   :func:`check_errors` whenever convenient to raise for any recorded error.
+  A rejected append batch writes nothing, and while a slot / position /
+  duplicate error is pending on the device (until :func:`check_errors`
+  clears it) every later append on that device is refused as well, so a bad
+  batch never leads to a partly written cache.
 """
 from __future__ import annotations
 
@@ -87,10 +92,34 @@ def check_errors(device: torch.device | int | None = None) -> None:
     raise_for_bits(read_and_clear(error_word(device)))
 
 
+_capability: dict = {}
+
+
 def require_sm100(device: torch.device) -> None:
-    cap = torch.cuda.get_device_capability(device)
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    cap = _capability.get(idx)
+    if cap is None:
+        cap = _capability[idx] = torch.cuda.get_device_capability(idx)
     if cap[0] != 10:
         raise RuntimeError(f"iris_kernel is built for sm_100a (B200); device capability is {cap}")
+
+
+_scratch: dict = {}
+
+
+def scratch(device: torch.device, stream: int, kind: str, nbytes: int) -> torch.Tensor:
+    """A device byte buffer of at least ``nbytes`` for one launcher on one
+    stream, kept between calls (the kernels rewrite what they read, so its
+    contents do not matter); one per stream so that calls in flight at the
+    same time never share it."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    key = (idx, stream, kind)
+    with _words_lock:
+        buf = _scratch.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=torch.device("cuda", idx))
+            _scratch[key] = buf
+    return buf
 
 
 def stream_ptr(device: torch.device) -> int:

@@ -97,7 +97,7 @@ def _launch(query, k_data, v_data, k_scale, v_scale, block_table, seq_lens, out,
         if not seq_lens.is_contiguous():
             seq_lens = seq_lens.contiguous()
         ws_bytes = _lib.lib.iris_b200_decode_workspace_bytes(batch, hq, hkv, head_dim, device.index or 0)
-        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
+        ws = _runtime.scratch(device, stream, "decode", ws_bytes)
         _lib.check_status(
             _lib.lib.iris_b200_int4_paged_decode(
                 query.data_ptr(), k_data.data_ptr(), v_data.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(),

@@ -125,14 +125,14 @@ def fused_rope_int4_paged_append(
         stream = _runtime.stream_ptr(device)
         word = _runtime.error_word(device)
         ws_bytes = _lib.lib.iris_b200_append_check_workspace_bytes(num_pages, page_size)
-        ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=device)
+        ws = _runtime.scratch(device, stream, "append_check", max(ws_bytes, 4))
         _lib.check_status(
             _lib.lib.iris_b200_append_check(positions.data_ptr(), slot_mapping.data_ptr(), num_tokens,
                                             cos_cache.shape[0], num_pages, page_size, ws.data_ptr(), ws.numel(),
                                             word.data_ptr(), stream),
             "iris_b200_append_check")
-        if _runtime.validation_mode() == "sync":
-            _runtime.raise_for_bits(_runtime.read_and_clear(word))
+        # the append kernel writes nothing if the check recorded an error, so
+        # one host read after both launches keeps "raise before writing"
         _lib.check_status(
             _lib.lib.iris_b200_rope_int4_paged_append(
                 key.data_ptr(), value.data_ptr(), positions.data_ptr(), slot_mapping.data_ptr(),
@@ -140,3 +140,5 @@ def fused_rope_int4_paged_append(
                 k_scale.data_ptr(), v_scale.data_ptr(), num_tokens, num_kv_heads, head_dim, cos_cache.shape[0],
                 num_pages, page_size, word.data_ptr(), stream),
             "iris_b200_rope_int4_paged_append")
+        if _runtime.validation_mode() == "sync":
+            _runtime.raise_for_bits(_runtime.read_and_clear(word))

@@ -209,28 +209,39 @@ def test_errors_raise_reference_types_and_leave_cache_untouched(bad, exc):
         assert torch.equal(t[k], before[k])
 
 
-def test_deferred_validation_records_and_skips():
+def test_deferred_validation_records_and_rejects_the_batch():
+    """Deferred mode: no host sync in the call; the bad batch is recorded and,
+    as in the reference (which raises before writing), nothing of it is
+    written.  Until check_errors() clears the record, later appends on the
+    device are refused too; after it, they write normally."""
     import iris_kernel
     from iris_kernel.fused_kv import fused_rope_int4_paged_append
 
     c = _small_case()
-    c["slot_mapping"] = np.array([17, 2, -1, 31, 99, 47, 63], np.int32)  # one slot out of range
-    t = to_dev(c, cases.APPEND_KEYS)
+    good = to_dev(c, cases.APPEND_KEYS)
+    bad_c = dict(c)
+    bad_c["slot_mapping"] = np.array([17, 2, -1, 31, 99, 47, 63], np.int32)  # one slot out of range
+    t = to_dev(bad_c, cases.APPEND_KEYS)
+    before = {k: t[k].clone() for k in CACHE}
+    good_before = {k: good[k].clone() for k in CACHE}
     iris_kernel.set_validation_mode("deferred")
     try:
         fused_rope_int4_paged_append(*[t[k] for k in cases.APPEND_KEYS], rotary_dim=128, page_size=16)
+        fused_rope_int4_paged_append(*[good[k] for k in cases.APPEND_KEYS], rotary_dim=128, page_size=16)
+        torch.cuda.synchronize()
+        for k in CACHE:
+            assert torch.equal(t[k], before[k])  # rejected batch: untouched
+            assert torch.equal(good[k], good_before[k])  # refused while the error is pending
         with pytest.raises(IndexError):
             iris_kernel.check_errors()
         iris_kernel.check_errors()  # cleared
+        fused_rope_int4_paged_append(*[good[k] for k in cases.APPEND_KEYS], rotary_dim=128, page_size=16)
+        iris_kernel.check_errors()
     finally:
         iris_kernel.set_validation_mode("sync")
-    # the valid tokens were written exactly as the oracle writes them
-    ok = c["slot_mapping"] < 64
-    ref_c = dict(c)
-    ref_c["slot_mapping"] = np.where(ok, c["slot_mapping"], -1).astype(np.int32)
-    ref = _oracle(ref_c)
+    ref = _oracle(c)
     for k in CACHE:
-        assert t[k].cpu().numpy().tobytes() == ref[k].tobytes()
+        assert good[k].cpu().numpy().tobytes() == ref[k].tobytes()
 
 
 def test_unsupported_shapes_raise():
