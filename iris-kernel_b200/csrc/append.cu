@@ -200,10 +200,6 @@ __global__ void __launch_bounds__(AppendCfg<D>::kThreads) rope_int4_append_kerne
   const uint32_t tok = p.heads_div.div(row);
   const uint32_t h = row - tok * static_cast<uint32_t>(p.num_heads);
 
-  // A slot / position / duplicate error already recorded (by the check
-  // kernel that runs first) means the batch is rejected: write nothing, as
-  // the reference raises before it writes.
-  if (p.err != nullptr && (*p.err & kRejectBits) != 0) return;
   const int32_t slot = __ldg(p.slots + tok);
   if (slot < 0) return;
   const int32_t pos = __ldg(p.positions + tok);
@@ -260,6 +256,12 @@ __global__ void __launch_bounds__(AppendCfg<D>::kThreads) rope_int4_append_kerne
   uint4 kw, vw;
   quant_group(kr, ks, kw);
   quant_group(vo, vs, vw);
+  // Everything above overlaps the check kernel (programmatic launch); the
+  // stores wait for it.  A slot / position / duplicate error it recorded
+  // means the batch is rejected: nothing is written, as the reference raises
+  // before it writes.
+  grid_dependency_wait();
+  if (p.err != nullptr && (*p.err & kRejectBits) != 0) return;
   const uint32_t page = p.page_div.div(static_cast<uint32_t>(slot));
   const uint32_t off = static_cast<uint32_t>(slot) - page * static_cast<uint32_t>(p.page_size);
   const size_t crow_idx = (static_cast<size_t>(page) * p.page_size + off) * p.num_heads + h;  // cache row
@@ -274,6 +276,7 @@ __global__ void __launch_bounds__(AppendCfg<D>::kThreads) rope_int4_append_kerne
 __global__ void append_check_kernel(const int32_t* __restrict__ positions, const int32_t* __restrict__ slots,
                                     int64_t num_tokens, int64_t max_position, int64_t num_slots,
                                     uint32_t* __restrict__ bitmap, int32_t* err) {
+  grid_dependents_launch();  // the append kernel may start loading meanwhile
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= num_tokens) return;
   const int32_t s = slots[i];
@@ -298,8 +301,18 @@ static cudaError_t launch_append(const AppendParams& p, cudaStream_t stream) {
   const int64_t blocks = (rows + C::kRows - 1) / C::kRows;
   if (blocks == 0) return cudaSuccess;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
-  rope_int4_append_kernel<D><<<static_cast<unsigned>(blocks), C::kThreads, 0, stream>>>(p);
-  return cudaGetLastError();
+  // programmatic launch: starts while the check kernel before it finishes
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, rope_int4_append_kernel<D>, p);
 }
 
 }  // namespace iris

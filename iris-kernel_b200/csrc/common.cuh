@@ -139,6 +139,15 @@ IRIS_DEV void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// ------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while
+// the previous kernel of the stream is still running (once every CTA of that
+// kernel has called grid_dependents_launch, or exited); grid_dependency_wait
+// then blocks until the previous kernel has finished and its memory writes
+// are visible.  Without the launch attribute both are no-ops.
+IRIS_DEV void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+IRIS_DEV void grid_dependents_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------- warp-level matrix
 IRIS_DEV void ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"

@@ -586,6 +586,7 @@ __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ CUtensorM
                                                         const __grid_constant__ CUtensorMap vmap,
                                                         const DecodeParams p) {
   using C = DecCfg<D>;
+  grid_dependents_launch();  // the combine kernel may launch and wait meanwhile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
@@ -1036,6 +1037,7 @@ __global__ void __maxnreg__(128) decode_pair_kernel(const __grid_constant__ CUte
                                                              const DecodeParams p) {
   using C = DecCfg<D>;
   constexpr int CW = 8 / HP;
+  grid_dependents_launch();  // the combine kernel may launch and wait meanwhile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
@@ -1152,6 +1154,7 @@ __global__ void __maxnreg__(128) decode_pair_kernel(const __grid_constant__ CUte
 // were written by the decode kernel and are skipped.
 template <int D>
 __global__ void __launch_bounds__(D / 4) decode_combine_kernel(const DecodeParams p) {
+  grid_dependency_wait();  // records, prefix sums and (U, R) come from the decode kernel
   const int b = blockIdx.x, qh = blockIdx.y, t = threadIdx.x;
   const int64_t U = p.meta[0], R = p.meta[1];
   const int64_t ps = p.prefix[b], pe = p.prefix[b + 1];
@@ -1502,9 +1505,19 @@ cudaError_t launch_decode(const Plan& pl, const CUtensorMap& km, const CUtensorM
     record_cuda_error(e, "decode_kernel launch");
     return e;
   }
-  dim3 cgrid(p.batch, p.hq);
-  decode_combine_kernel<D><<<cgrid, D / 4, 0, stream>>>(p);
-  e = cudaGetLastError();
+  // programmatic launch: the combine CTAs are resident before the decode ends
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.batch, p.hq);
+  cfg.blockDim = dim3(D / 4);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, decode_combine_kernel<D>, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) record_cuda_error(e, "decode_combine_kernel launch");
   return e;
 }
