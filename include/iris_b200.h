@@ -108,6 +108,22 @@ IRIS_API int iris_b200_rope_int4_paged_append(const void* key, const void* value
                                      int32_t num_kv_heads, int32_t head_dim, int64_t max_position,
                                      int64_t num_pages, int32_t page_size, int32_t* error_word, void* stream);
 
+/*
+ * Group-32 symmetric INT4 quantisation + low-nibble-first packing of a
+ * contiguous fp16 tensor, without RoPE or paging.  Replaces the
+ * _quantize_pack_int4_g32 launch of fused_quantize_pack_int4
+ * (fused_kv.py:300-416); bit-exact with quantize_int4_groupwise + pack_int4
+ * (torch_eager_kv.py:52-107).
+ *
+ *   x      [rows, head_dim] fp16 (rows = T * H), 16-byte aligned
+ *   packed [rows, head_dim/2] uint8, 16-byte aligned
+ *   scales [rows, head_dim/32] fp16
+ *   head_dim a multiple of 32 (the Python wrapper keeps the reference's
+ *   multiple-of-64 rule).
+ */
+IRIS_API int iris_b200_int4_quantize_pack(const void* x, void* packed, void* scales, int64_t rows, int32_t head_dim,
+                                          void* stream);
+
 /* ======================================================================
  * READ PATH
  * ====================================================================== */

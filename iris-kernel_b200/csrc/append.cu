@@ -294,6 +294,25 @@ __global__ void append_check_kernel(const int32_t* __restrict__ positions, const
   if (bits) set_error(err, bits);
 }
 
+// Standalone group-32 INT4 quantise + pack of a contiguous [rows, D] fp16
+// tensor (rows = T * H): the append's quantiser without RoPE or paging.  One
+// thread per 32-value group: 64 bytes in, 16 packed bytes + one fp16 scale
+// out.
+__global__ void __launch_bounds__(256) quantize_pack_kernel(const __half* __restrict__ x, uint8_t* __restrict__ packed,
+                                                            __half* __restrict__ scales, int64_t groups) {
+  const int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (g >= groups) return;
+  const __half* src = x + g * 32;
+  uint4 v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = ldg_nc_v4(src + 8 * i);
+  __half sc;
+  uint4 w;
+  quant_group(v, sc, w);
+  *reinterpret_cast<uint4*>(packed + g * 16) = w;
+  scales[g] = sc;
+}
+
 template <int D>
 static cudaError_t launch_append(const AppendParams& p, cudaStream_t stream) {
   using C = AppendCfg<D>;
@@ -409,6 +428,27 @@ extern "C" int iris_b200_rope_int4_paged_append(const void* key, const void* val
   }
   if (e != cudaSuccess) {
     record_cuda_error(e, "rope_int4_append_kernel launch");
+    return IRIS_ECUDA;
+  }
+  return IRIS_OK;
+}
+
+extern "C" int iris_b200_int4_quantize_pack(const void* x, void* packed, void* scales, int64_t rows, int32_t head_dim,
+                                            void* stream) {
+  if (rows < 0 || head_dim <= 0 || head_dim % 32 != 0) return IRIS_EINVAL;
+  if (rows == 0) return IRIS_OK;
+  if (x == nullptr || packed == nullptr || scales == nullptr) return IRIS_EINVAL;
+  if (!aligned(x, 16) || !aligned(packed, 16) || !aligned(scales, 2)) return IRIS_EALIGN;
+  const int64_t groups = rows * (head_dim / 32);
+  const int threads = 256;
+  const int64_t blocks = (groups + threads - 1) / threads;
+  if (blocks > 0x7fffffffLL) return IRIS_EUNSUPPORTED;
+  clear_stale_cuda_error();
+  quantize_pack_kernel<<<static_cast<unsigned>(blocks), threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(x), static_cast<uint8_t*>(packed), static_cast<__half*>(scales), groups);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    record_cuda_error(e, "quantize_pack_kernel launch");
     return IRIS_ECUDA;
   }
   return IRIS_OK;

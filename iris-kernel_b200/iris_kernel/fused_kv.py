@@ -142,3 +142,48 @@ def fused_rope_int4_paged_append(
             "iris_b200_rope_int4_paged_append")
         if _runtime.validation_mode() == "sync":
             _runtime.raise_for_bits(_runtime.read_and_clear(word))
+
+
+def fused_quantize_pack_int4(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor) -> None:
+    """Group-32 INT4 quantisation + low-nibble-first packing of ``x [T, H, D]``
+    fp16 into ``packed [T, H, D/2]`` uint8 and ``scales [T, H, D/32]`` fp16,
+    in place.  Drop-in for fused_kv.py:362-416 of the reference (same checks,
+    messages and exception types); bit-exact with its eager
+    ``quantize_int4_groupwise`` + ``pack_int4``.  Tensors must be contiguous."""
+    if not torch.cuda.is_available():
+        raise RuntimeError("Iris fused kernels require CUDA")
+    if x.device.type != "cuda":
+        raise ValueError("x must be a CUDA tensor")
+    if x.ndim != 3:
+        raise ValueError("x must have shape [T, H_kv, D]")
+    if x.dtype != torch.float16:
+        raise TypeError("INT4 fast path currently requires FP16 input")
+    _, _, head_dim = x.shape
+    if head_dim % 64 != 0:
+        raise NotImplementedError("INT4 fast path currently requires head_dim divisible by 64")
+    expected_packed = (x.shape[0], x.shape[1], head_dim // 2)
+    expected_scales = (x.shape[0], x.shape[1], head_dim // 32)
+    if tuple(packed.shape) != expected_packed:
+        raise ValueError(f"packed tensor must have shape {expected_packed}")
+    if tuple(scales.shape) != expected_scales:
+        raise ValueError(f"scales must have shape {expected_scales}")
+    if packed.dtype != torch.uint8:
+        raise TypeError("packed tensor must use UINT8(torch.uint8)")
+    if scales.dtype != torch.float16:
+        raise TypeError("scales must use FP16(torch.float16)")
+    if packed.device != x.device:
+        raise ValueError("packed tensor must be on the same device as x")
+    if scales.device != x.device:
+        raise ValueError("scales must be on the same device as x")
+    for name, t in (("x", x), ("packed", packed), ("scales", scales)):
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    _runtime.require_sm100(x.device)
+    rows = x.shape[0] * x.shape[1]
+    if rows == 0:
+        return
+    with torch.cuda.device(x.device):
+        _lib.check_status(
+            _lib.lib.iris_b200_int4_quantize_pack(x.data_ptr(), packed.data_ptr(), scales.data_ptr(), rows, head_dim,
+                                                  _runtime.stream_ptr(x.device)),
+            "iris_b200_int4_quantize_pack")
