@@ -56,6 +56,7 @@ OUTLIER_CH = (3, 40, 77, 121)
 DECODE_BYTES = B * L * HKV * (D + D // 8) + 2 * B * HQ * D * 2 + B * (L // P + 1) * 4
 APPEND_BYTES = B * HKV * (4 * D + D + D // 8) + B * 8 + 2 * (D // 2) * 2
 STEP_BYTES = DECODE_BYTES + APPEND_BYTES
+FP16_BYTES = B * L * HKV * D * 2 * 2 + 2 * B * HQ * D * 2 + B * (L // P + 1) * 4
 SPEC_TBS = 8.0
 
 # BASELINE config 5b: prefill-style append, 8 sequences x 8192 new tokens,
@@ -492,6 +493,17 @@ def main():
     ms_c4 = timed(g_c4.replay, x_steps, dev, dist, args.warmup)
     iris_kernel.check_errors(dev)
     del g_c4, dec4, c4  # the graph holds an NCCL call: released before the process group
+    # the matched FP16 decode on the config-2 shape (the INT4 cache's baseline)
+    from iris_kernel.fused_attention import fused_fp16_paged_decode_attention
+
+    g16 = torch.Generator(device=dev).manual_seed(16 + rank)
+    kc = (torch.randn(POOL, P, HKV, D, generator=g16, device=dev) * 0.5).half()
+    vc = (torch.randn(POOL, P, HKV, D, generator=g16, device=dev) * 0.5).half()
+    out16 = torch.empty_like(w["q"])
+    g_f16 = graph_of(lambda: fused_fp16_paged_decode_attention(w["q"], kc, vc, w["bt"], w["lens"], out16), dev)
+    ms_f16 = timed(g_f16.replay, x_steps, dev, dist, args.warmup)
+    iris_kernel.check_errors(dev)
+    del g_f16, kc, vc
     # config 3: sequence-sharded MHA decode, no collective
     c3 = build_c3(dev, rank, world, seed=33 + rank)
     g_c3 = graph_of(lambda: fused_int4_paged_decode_attention(c3["q"], c3["kd"], c3["vd"], c3["ks"], c3["vs"],
@@ -501,6 +513,7 @@ def main():
     iris_kernel.set_validation_mode("sync")
     c3_total = c3["total_bytes"]
     del g_c3, c3
+    f16_us = max_over_ranks(ms_f16, dist, dev) / x_steps * 1e3
     c4_us = max_over_ranks(ms_c4, dist, dev) / x_steps * 1e3
     c3_us = max_over_ranks(ms_c3, dist, dev) / x_steps * 1e3
     ms = max_over_ranks(ms, dist, dev)
@@ -607,6 +620,10 @@ def main():
                 "us": c4_us, "tbs": C4_BYTES / (c4_us * 1e-6) / 1e12, "bytes": C4_BYTES,
                 "collective": "one NCCL all_gather_into_tensor of packed (O, lse) fp32 per step" if world > 1
                               else "none (one GPU)"},
+            "fp16_decode_c2": {
+                "config": "matched FP16 paged decode on the config-2 shape (64 x 4096, Hq 32, Hkv 8, D 128)",
+                "us": f16_us, "tbs": FP16_BYTES / (f16_us * 1e-6) / 1e12, "bytes": FP16_BYTES,
+                "int4_speedup": f16_us / dec_us},
             "config3_sharded": {
                 "config": "BASELINE config 3: 128 sequences, L ~ U[1,16384] (seed 1), Hq = Hkv = 16, D 64; "
                           "whole sequences sharded over the ranks by token count, no collective",

@@ -165,6 +165,28 @@ IRIS_API int iris_b200_int4_paged_decode(const void* query, const void* k_data, 
                                 float softmax_scale, void* workspace, size_t workspace_bytes, int32_t* error_word,
                                 void* stream);
 
+/* Bytes of device workspace iris_b200_fp16_paged_decode needs. */
+IRIS_API size_t iris_b200_fp16_decode_workspace_bytes(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                                                      int32_t head_dim, int32_t device);
+
+/*
+ * Matched FP16 paged decode attention (the INT4 decode's baseline).
+ * Replaces the _fp16_paged_decode_attention launch of
+ * fused_attention.py:528-582 with the semantics of
+ * torch_eager_fp16_paged_decode_attention (torch_eager_attention.py:243-294):
+ * softmax(scale * q.k) v over the sequence's fp16 K/V, FP32 accumulation.
+ * Same schedule, workspace rules, outputs and error word as
+ * iris_b200_int4_paged_decode, with
+ *   k_cache, v_cache [num_pages, 16, Hkv, D] fp16, 16-byte aligned.
+ */
+IRIS_API int iris_b200_fp16_paged_decode(const void* query, const void* k_cache, const void* v_cache,
+                                         const int32_t* block_table, int64_t block_table_stride,
+                                         const int32_t* seq_lens, void* output, float* out_lse, int32_t out_mode,
+                                         int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                         int64_t num_pages, int32_t page_size, int32_t max_pages_per_seq,
+                                         float softmax_scale, void* workspace, size_t workspace_bytes,
+                                         int32_t* error_word, void* stream);
+
 /* Size of the scratch array iris_b200_int4_paged_decode_noalloc uses (32 MiB). */
 #define IRIS_DECODE_NOALLOC_SCRATCH_BYTES (32u << 20)
 

@@ -500,19 +500,38 @@ IRIS_DEV void finish_piece(const DecodeParams& p, WarpState<D, NT>& st, int b, i
 // waits for free ring stages and issues, per page, one 4-D TMA copy per
 // tensor for the CTA's HB heads plus the page's two scale blocks.  Returns
 // once every copy it issued has landed (or a bounded wait gave up).
-template <int D>
+// How a stage's tiles are fetched: the INT4 cache (4-D box per tensor plus
+// the page's two scale blocks) or the FP16 cache (4-D box at D = 64, 5-D box
+// of two 128-byte halves per row at D = 128; no scales).
+struct Int4Copy {
+  static constexpr bool kScales = true;
+  IRIS_DEV static void load(void* dst, const CUtensorMap* m, int head0, int pid, uint64_t* bar) {
+    tma_load_4d(dst, m, 0, 0, head0, pid, bar);
+  }
+};
+template <int kDims>
+struct Fp16Copy {
+  static constexpr bool kScales = false;
+  IRIS_DEV static void load(void* dst, const CUtensorMap* m, int head0, int pid, uint64_t* bar) {
+    if constexpr (kDims == 5)
+      tma_load_5d(dst, m, 0, 0, 0, head0, pid, bar);
+    else
+      tma_load_4d(dst, m, 0, 0, head0, pid, bar);
+  }
+};
+
+template <typename Copy, int kTile>
 IRIS_DEV void run_producer(const CUtensorMap* kmap_p, const CUtensorMap* vmap_p, const DecodeParams& p,
                            uint8_t* smem, int stage_bytes, int S, int HB, int hblk, int64_t u0, int64_t u1,
                            int b_first, int64_t ps_first, uint64_t* full, uint32_t full_u32, uint32_t empty_u32,
                            int scale_block, int lane) {
-  using C = DecCfg<D>;
   // All lanes fetch (and validate) page ids 32 at a time, one chunk ahead
   // of lane 0, which waits for free stages and issues the copies.
   if (lane == 0) {
     prefetch_tensormap(kmap_p);
     prefetch_tensormap(vmap_p);
   }
-  const uint32_t tx = 2 * HB * C::kTileBytes + 2 * scale_block;
+  const uint32_t tx = 2 * HB * kTile + (Copy::kScales ? 2 * scale_block : 0);
   uint32_t issued = 0;
   int s = 0;          // stage of the next page
   uint32_t ph = 0;    // its ring pass parity
@@ -554,11 +573,14 @@ IRIS_DEV void run_producer(const CUtensorMap* kmap_p, const CUtensorMap* vmap_p,
           } else {
             uint8_t* st = smem + s * stage_bytes;
             mbar_arrive_expect_tx(full + s, tx);
-            tma_load_4d(st, kmap_p, 0, 0, hblk * HB, pid, full + s);
-            tma_load_4d(st + HB * C::kTileBytes, vmap_p, 0, 0, hblk * HB, pid, full + s);
-            uint8_t* sc = st + 2 * HB * C::kTileBytes;
-            bulk_g2s(sc, p.k_scale + static_cast<int64_t>(pid) * scale_block, scale_block, full + s);
-            bulk_g2s(sc + scale_block, p.v_scale + static_cast<int64_t>(pid) * scale_block, scale_block, full + s);
+            Copy::load(st, kmap_p, hblk * HB, pid, full + s);
+            Copy::load(st + HB * kTile, vmap_p, hblk * HB, pid, full + s);
+            if constexpr (Copy::kScales) {
+              uint8_t* sc = st + 2 * HB * kTile;
+              bulk_g2s(sc, p.k_scale + static_cast<int64_t>(pid) * scale_block, scale_block, full + s);
+              bulk_g2s(sc + scale_block, p.v_scale + static_cast<int64_t>(pid) * scale_block, scale_block,
+                       full + s);
+            }
             ++issued;
           }
         }
@@ -621,8 +643,8 @@ __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ CUtensorM
   const uint32_t full_u32 = smem_u32(full), empty_u32 = smem_u32(empty);
 
   if (warp == HB) {
-    run_producer<D>(&kmap, &vmap, p, smem, stage_bytes, S, HB, hblk, u0, u1, b_first, ps_first, full, full_u32,
-                    empty_u32, scale_block, lane);
+    run_producer<Int4Copy, C::kTileBytes>(&kmap, &vmap, p, smem, stage_bytes, S, HB, hblk, u0, u1, b_first, ps_first,
+                                          full, full_u32, empty_u32, scale_block, lane);
     return;
   }
 
@@ -1076,8 +1098,8 @@ __global__ void __maxnreg__(128) decode_pair_kernel(const __grid_constant__ CUte
   const uint32_t full_u32 = smem_u32(full), empty_u32 = smem_u32(empty);
 
   if (warp == NW) {
-    run_producer<D>(&kmap, &vmap, p, smem, stage_bytes, S, HB, hblk, u0, u1, b_first, ps_first, full, full_u32,
-                    empty_u32, scale_block, lane);
+    run_producer<Int4Copy, C::kTileBytes>(&kmap, &vmap, p, smem, stage_bytes, S, HB, hblk, u0, u1, b_first, ps_first,
+                                          full, full_u32, empty_u32, scale_block, lane);
     return;
   }
 
@@ -1142,6 +1164,311 @@ __global__ void __maxnreg__(128) decode_pair_kernel(const __grid_constant__ CUte
     const bool complete = (ps >= u0) && (pe <= u1);
     const int64_t rec = static_cast<int64_t>(r) * 2 + (u == u0 ? 0 : 1);
     pair_finish_piece<D, HP>(p, st, b, kv0, complete, rec, lane);
+    u = hi;
+    ps = pe;
+    ++b;
+  }
+}
+
+// ------------------------------------------------------- FP16 cache decode
+// The matched FP16 baseline (reference fused_attention.py:223-370,528-582):
+// k_cache / v_cache [pages, 16, Hkv, D] fp16.  Same split-KV schedule,
+// producer and combine as the INT4 decode; a stage holds each head's K and V
+// tile as [D/64 halves][16 tokens][128 bytes], 128-byte swizzled, so the
+// consumer reads MMA fragments with ldmatrix (K) and ldmatrix.trans (V)
+// without conversions.  One KV head per consumer warp, NT n-tiles of 8
+// query heads.
+
+template <int D>
+struct Fp16Cfg {
+  static constexpr int kTileBytes = kPage * D * 2;  // one head's K (or V) tile of a page
+  static constexpr int kHalves = D / 64;            // 128-byte rows per token
+};
+
+template <int D, int NT>
+struct Fp16State {
+  float o[NT][D / 16][4];
+  float m[NT][2];
+  float l[NT][2];
+  uint32_t qf[NT][D / 16][2];  // Q as mma B fragments
+};
+
+// Byte offset of 16-byte chunk `chunk` of token row `tok` in half `half` of a
+// tile (128-byte swizzle: chunk index XOR token & 7).
+IRIS_DEV uint32_t fp16_tile_off(int half, int tok, int chunk) {
+  return (half * kPage + tok) * 128 + ((chunk ^ (tok & 7)) << 4);
+}
+
+template <int D, int NT>
+IRIS_DEV void fp16_load_query(Fp16State<D, NT>& st, const __half* __restrict__ q_seq, int qpk, int lane) {
+  const int n = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int qh = nt * 8 + n;
+    const __half* q = q_seq + qh * D;
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      uint32_t b0 = 0, b1 = 0;
+      if (qh < qpk) {
+        b0 = *reinterpret_cast<const uint32_t*>(q + 16 * ks + 2 * t);
+        b1 = *reinterpret_cast<const uint32_t*>(q + 16 * ks + 8 + 2 * t);
+      }
+      st.qf[nt][ks][0] = b0;
+      st.qf[nt][ks][1] = b1;
+    }
+#pragma unroll
+    for (int i = 0; i < D / 16; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) st.o[nt][i][j] = 0.f;
+    st.m[nt][0] = st.m[nt][1] = 0.f;  // replaced by the first page's maxima
+    st.l[nt][0] = st.l[nt][1] = 0.f;
+  }
+}
+
+// One page of this warp's head: lazy online softmax as in pair_process_page.
+// Tokens >= valid (MASK) are masked, and their V rows are zeroed in shared
+// memory first (the cache may hold anything there, even NaN).
+template <int D, int NT, bool MASK>
+IRIS_DEV void fp16_process_page(Fp16State<D, NT>& st, uint32_t ktile, uint32_t vtile, uint8_t* vtile_ptr, int valid,
+                                float scale_log2, bool first, int lane) {
+  const int g8 = lane >> 2;
+  const int mat = lane >> 3;
+  // ---- scores: S^T[tok][qh] = K . Q^T, two accumulator chains ----
+  float s[NT][4];
+  {
+    float acc[NT][2][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[nt][c][j] = 0.f;
+    const int tok = (lane & 7) + 8 * (mat & 1);
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      uint32_t a[4];
+      ldmatrix_x4(a, ktile + fp16_tile_off(ks / 4, tok, 2 * (ks % 4) + (mat >> 1)));
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) mma_16816(acc[nt][ks & 1], a, st.qf[nt][ks][0], st.qf[nt][ks][1], acc[nt][ks & 1]);
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s[nt][j] = acc[nt][0][j] + acc[nt][1][j];
+  }
+  if (MASK) {
+    // zero the V rows of tokens past the end (lanes split the rows' 16-byte chunks)
+    constexpr int kChunks = kPage * (D / 8);  // 16-byte chunks in a V tile
+    for (int c = lane; c < kChunks; c += 32) {
+      const int row = c / (D / 8);  // token
+      if (row >= valid) {
+        const int ch = c % (D / 8);
+        *reinterpret_cast<uint4*>(vtile_ptr + fp16_tile_off(ch / 8, row, ch % 8)) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    fence_proxy_async_shared();
+    __syncwarp();
+  }
+  float pr[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    float y[4];
+    y[0] = fmaf(s[nt][0], scale_log2, -st.m[nt][0]);
+    y[1] = fmaf(s[nt][1], scale_log2, -st.m[nt][1]);
+    y[2] = fmaf(s[nt][2], scale_log2, -st.m[nt][0]);
+    y[3] = fmaf(s[nt][3], scale_log2, -st.m[nt][1]);
+    if (MASK) {
+      if (g8 >= valid) y[0] = y[1] = kNegInf;
+      if (g8 + 8 >= valid) y[2] = y[3] = kNegInf;
+    }
+    float mx0 = fmaxf(y[0], y[2]), mx1 = fmaxf(y[1], y[3]);
+    if (__any_sync(0xffffffffu, first || fmaxf(mx0, mx1) > 8.0f)) {
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+      }
+      const float inc0 = first ? mx0 : fmaxf(mx0, 0.f), inc1 = first ? mx1 : fmaxf(mx1, 0.f);
+      st.m[nt][0] += inc0;
+      st.m[nt][1] += inc1;
+      y[0] -= inc0;
+      y[1] -= inc1;
+      y[2] -= inc0;
+      y[3] -= inc1;
+      if (!first) {
+        const float c0 = ex2(-inc0), c1 = ex2(-inc1);
+#pragma unroll
+        for (int i = 0; i < D / 16; ++i) {
+          st.o[nt][i][0] *= c0;
+          st.o[nt][i][1] *= c1;
+          st.o[nt][i][2] *= c0;
+          st.o[nt][i][3] *= c1;
+        }
+        st.l[nt][0] *= c0;
+        st.l[nt][1] *= c1;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) pr[nt][k] = ex2(y[k]);
+    st.l[nt][0] += pr[nt][0] + pr[nt][2];
+    st.l[nt][1] += pr[nt][1] + pr[nt][3];
+  }
+  // ---- O^T += V^T . P^T ----
+  uint32_t pb[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    pb[nt][0] = movmatrix_trans(h2_as_u32(__floats2half2_rn(pr[nt][0], pr[nt][1])));
+    pb[nt][1] = movmatrix_trans(h2_as_u32(__floats2half2_rn(pr[nt][2], pr[nt][3])));
+  }
+  const int vtok = (lane & 7) + 8 * (mat >> 1);
+#pragma unroll
+  for (int i = 0; i < D / 16; ++i) {
+    uint32_t a[4];
+    ldmatrix_x4_trans(a, vtile + fp16_tile_off(i / 4, vtok, 2 * (i % 4) + (mat & 1)));
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) mma_16816(st.o[nt][i], a, pb[nt][0], pb[nt][1], st.o[nt][i]);
+  }
+}
+
+// Output (or record) of a piece: O^T rows are head dims 16i + g8 (+8).
+template <int D, int NT>
+IRIS_DEV void fp16_finish_piece(const DecodeParams& p, Fp16State<D, NT>& st, int b, int kvh, bool complete,
+                                int64_t rec, int lane) {
+  const int g8 = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    float l0 = st.l[nt][0], l1 = st.l[nt][1];
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+    }
+    const float inv[2] = {1.0f / l0, 1.0f / l1};
+    const float lse[2] = {st.m[nt][0] + lg2(l0), st.m[nt][1] + lg2(l1)};
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int qh_local = nt * 8 + 2 * t + j;
+      if (qh_local >= p.qpk) continue;
+      const int qh = kvh * p.qpk + qh_local;
+      const int64_t row = complete ? static_cast<int64_t>(b) * p.hq + qh : rec * p.hq + qh;
+#pragma unroll
+      for (int i = 0; i < D / 16; ++i) {
+        const float v0 = st.o[nt][i][j] * inv[j], v1 = st.o[nt][i][2 + j] * inv[j];
+        const int d = 16 * i + g8;
+        if (complete && p.out_mode == IRIS_DECODE_OUT_FP16) {
+          __half* dst = static_cast<__half*>(p.out) + row * D;
+          dst[d] = __float2half_rn(v0);
+          dst[d + 8] = __float2half_rn(v1);
+        } else {
+          float* dst = (complete ? static_cast<float*>(p.out) : p.rec_o) + row * D;
+          dst[d] = v0;
+          dst[d + 8] = v1;
+        }
+      }
+      if (g8 == 0) {
+        if (complete) {
+          if (p.out_mode == IRIS_DECODE_OUT_LSE) p.out_lse[static_cast<int64_t>(b) * p.hq + qh] = lse[j];
+        } else {
+          p.rec_lse[rec * p.hq + qh] = lse[j];
+        }
+      }
+    }
+  }
+}
+
+template <int D, int NT>
+__global__ void __maxnreg__(128) decode_fp16_kernel(const __grid_constant__ CUtensorMap kmap,
+                                                            const __grid_constant__ CUtensorMap vmap,
+                                                            const DecodeParams p) {
+  using C = Fp16Cfg<D>;
+  grid_dependents_launch();  // the combine kernel may launch and wait meanwhile
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  const int hblk = blockIdx.x;
+  const int r = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int HB = p.hb;
+  const int S = p.stages;
+  __shared__ CtaPlan plan;
+
+  const int stage_bytes = (2 * HB * C::kTileBytes + 1023) & ~1023;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * stage_bytes);
+  uint64_t* empty = full + S;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, HB);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 0) plan_cta(p, r, gridDim.y, blockIdx.x == 0 && r == 0, lane, &plan);
+  __syncthreads();
+  const int64_t U = plan.U;
+  const int R = plan.R;
+  if (r >= R) return;  // uniform per CTA (nothing was issued yet)
+
+  const int64_t u0 = range_start(r, U, R), u1 = range_start(r + 1, U, R);
+  const int b_first = plan.b_first;
+  const int64_t ps_first = plan.ps_first;
+  const uint32_t full_u32 = smem_u32(full), empty_u32 = smem_u32(empty);
+
+  if (warp == HB) {
+    run_producer<Fp16Copy<(D > 64) ? 5 : 4>, C::kTileBytes>(&kmap, &vmap, p, smem, stage_bytes, S, HB, hblk, u0, u1,
+                                                            b_first, ps_first, full, full_u32, empty_u32, 0, lane);
+    return;
+  }
+
+  // ========================= consumer warps =========================
+  const int kvh = hblk * HB + warp;
+  Fp16State<D, NT> st;
+  const uint32_t ring = smem_u32(smem);
+  const uint32_t k_off = warp * C::kTileBytes, v_off = (HB + warp) * C::kTileBytes;
+  int s = 0;
+  uint32_t ph = 0;
+  uint32_t stage = ring;
+  uint8_t* stage_ptr = smem;
+  int b = b_first;
+  int64_t ps = ps_first;
+  int64_t u = u0;
+  while (u < u1) {
+    const int64_t pe = ps + seq_pages(p, b);
+    if (pe <= u) {
+      ps = pe;
+      ++b;
+      continue;
+    }
+    const int64_t hi = pe < u1 ? pe : u1;
+    const int L = min(p.seq_lens[b], p.max_pages * kPage);
+    fp16_load_query<D, NT>(st, p.query + (static_cast<int64_t>(b) * p.hq + kvh * p.qpk) * D, p.qpk, lane);
+    int valid = L - static_cast<int>(u - ps) * kPage;
+    bool first = true;
+    for (int64_t left = hi - u; left > 0; --left) {
+      if (!mbar_wait_bounded(full_u32 + 8 * s, ph, p.err)) return;
+      if (valid >= kPage)
+        fp16_process_page<D, NT, false>(st, stage + k_off, stage + v_off, stage_ptr + v_off, valid, p.scale_log2,
+                                        first, lane);
+      else
+        fp16_process_page<D, NT, true>(st, stage + k_off, stage + v_off, stage_ptr + v_off, valid, p.scale_log2,
+                                       first, lane);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty_u32 + 8 * s);
+      first = false;
+      valid -= kPage;
+      if (++s == S) {
+        s = 0;
+        ph ^= 1;
+        stage = ring;
+        stage_ptr = smem;
+      } else {
+        stage += stage_bytes;
+        stage_ptr += stage_bytes;
+      }
+    }
+    const bool complete = (ps >= u0) && (pe <= u1);
+    const int64_t rec = static_cast<int64_t>(r) * 2 + (u == u0 ? 0 : 1);
+    fp16_finish_piece<D, NT>(p, st, b, kvh, complete, rec, lane);
     u = hi;
     ps = pe;
     ++b;
@@ -1265,13 +1592,40 @@ bool make_kv_map(CUtensorMap* map, const void* base, int D, int hkv, int hb, int
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Tensor maps are pure functions of (base, D, Hkv, head block, pages); the
+// FP16 cache [pages, 16, Hkv, D] fp16 viewed as (64 elements, 16 tokens,
+// D/64 halves, Hkv heads, pages) with 128-byte swizzle: a box of (64, 16,
+// D/64, hb, 1) lands as hb per-head tiles [D/64][16][128 B] (4-D without the
+// halves dimension at D = 64).
+bool make_fp16_map(CUtensorMap* map, const void* base, int D, int hkv, int hb, int64_t num_pages) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) return false;
+  const cuuint64_t row = static_cast<cuuint64_t>(hkv) * D * 2;  // bytes per token (all heads)
+  const cuuint32_t estr[5] = {1u, 1u, 1u, 1u, 1u};
+  if (D == 128) {
+    const cuuint64_t dims[5] = {64u, static_cast<cuuint64_t>(kPage), 2u, static_cast<cuuint64_t>(hkv),
+                                static_cast<cuuint64_t>(num_pages)};
+    const cuuint64_t strides[4] = {row, 128u, static_cast<cuuint64_t>(D) * 2, row * kPage};
+    const cuuint32_t box[5] = {64u, static_cast<cuuint32_t>(kPage), 2u, static_cast<cuuint32_t>(hb), 1u};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  }
+  const cuuint64_t dims[4] = {64u, static_cast<cuuint64_t>(kPage), static_cast<cuuint64_t>(hkv),
+                              static_cast<cuuint64_t>(num_pages)};
+  const cuuint64_t strides[3] = {row, static_cast<cuuint64_t>(D) * 2, row * kPage};
+  const cuuint32_t box[4] = {64u, static_cast<cuuint32_t>(kPage), static_cast<cuuint32_t>(hb), 1u};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Tensor maps are pure functions of (format, base, D, Hkv, head block, pages); the
 // last few are kept so that a decode loop over the same cache does not
 // re-encode them on every call.
-bool cached_kv_map(CUtensorMap* map, const void* base, int D, int hkv, int hb, int64_t num_pages) {
+bool cached_kv_map(CUtensorMap* map, int fmt, const void* base, int D, int hkv, int hb, int64_t num_pages) {
   struct Entry {
     const void* base;
-    int D, hkv, hb;
+    int fmt, D, hkv, hb;
     int64_t pages;
     CUtensorMap map;
   };
@@ -1283,16 +1637,17 @@ bool cached_kv_map(CUtensorMap* map, const void* base, int D, int hkv, int hb, i
     std::lock_guard<std::mutex> lock(mu);
     for (int i = 0; i < used; ++i) {
       const Entry& e = cache[i];
-      if (e.base == base && e.D == D && e.hkv == hkv && e.hb == hb && e.pages == num_pages) {
+      if (e.base == base && e.fmt == fmt && e.D == D && e.hkv == hkv && e.hb == hb && e.pages == num_pages) {
         *map = e.map;
         return true;
       }
     }
   }
-  if (!make_kv_map(map, base, D, hkv, hb, num_pages)) return false;
+  if (!(fmt == 0 ? make_kv_map(map, base, D, hkv, hb, num_pages) : make_fp16_map(map, base, D, hkv, hb, num_pages)))
+    return false;
   std::lock_guard<std::mutex> lock(mu);
   Entry& e = cache[next];
-  e = Entry{base, D, hkv, hb, num_pages, *map};
+  e = Entry{base, fmt, D, hkv, hb, num_pages, *map};
   next = (next + 1) % kEntries;
   if (used < kEntries) ++used;
   return true;
@@ -1325,6 +1680,7 @@ int max_hb(int dflt) {
 // The CTA shape of one decode problem.
 struct Plan {
   DecodeKernelFn fn;
+  int fp16;  // FP16 cache (decode_fp16_kernel): bigger tiles, no scale blocks
   int hp;    // KV heads per consumer warp
   int hb;    // KV heads per CTA (one TMA box)
   int nw;    // consumer warps = hb / hp
@@ -1333,6 +1689,7 @@ struct Plan {
 
 Plan make_plan(int D, int qpk, int hkv) {
   Plan pl;
+  pl.fp16 = 0;
   pl.hp = heads_per_warp(qpk, hkv);
   pl.pair = pl.hp > 1;
   const int cap = max_hb(pl.pair ? 8 : 4);
@@ -1356,6 +1713,30 @@ Plan make_plan(int D, int qpk, int hkv) {
 struct LaunchShape {
   int stages, stage_bytes, smem, ranges, max_ranges;
 };
+
+// FP16 cache: one KV head per consumer warp, at most 4 heads per CTA (a
+// stage holds 2 * 4 KB per head at D = 128).
+Plan make_plan_fp16(int D, int qpk, int hkv) {
+  Plan pl;
+  pl.fp16 = 1;
+  pl.hp = 1;
+  pl.pair = 0;
+  const int cap = max_hb(4);
+  pl.hb = 1;
+  for (int hb = cap; hb >= 1; hb >>= 1)
+    if (hkv % hb == 0) {
+      pl.hb = hb;
+      break;
+    }
+  pl.nw = pl.hb;
+  if (D == 128)
+    pl.fn = qpk <= 8 ? decode_fp16_kernel<128, 1> : decode_fp16_kernel<128, 2>;
+  else
+    pl.fn = qpk <= 8 ? decode_fp16_kernel<64, 1> : decode_fp16_kernel<64, 2>;
+  return pl;
+}
+
+int stage_bytes_fp16(int D, int hb) { return (2 * hb * kPage * D * 2 + 1023) & ~1023; }
 
 int stage_bytes_for(int D, int hkv, int hb) {
   const int tile = kPage * D / 2;
@@ -1390,8 +1771,8 @@ int target_ctas_per_sm(const Plan& pl) { return 16 / pl.nw < 1 ? 1 : 16 / pl.nw;
 
 // Upper bound on the number of ranges (sizes the workspace): at most 16
 // consumer warps' worth of CTAs per SM.
-int max_ranges_for(int qpk, int hkv, int sms) {
-  const Plan pl = make_plan(128, qpk, hkv);
+int max_ranges_for(int qpk, int hkv, int sms, bool fp16 = false) {
+  const Plan pl = fp16 ? make_plan_fp16(128, qpk, hkv) : make_plan(128, qpk, hkv);
   const int r = sms * target_ctas_per_sm(pl) / (hkv / pl.hb);
   return r < 1 ? 1 : r;
 }
@@ -1418,8 +1799,8 @@ LaunchShape compute_launch_shape(const Plan& pl, int D, int qpk, int hkv, int de
   LaunchShape s;
   const int sms = device_sms(device);
   const int nhb = hkv / pl.hb;
-  s.stage_bytes = stage_bytes_for(D, hkv, pl.hb);
-  s.max_ranges = max_ranges_for(qpk, hkv, sms);
+  s.stage_bytes = pl.fp16 ? stage_bytes_fp16(D, pl.hb) : stage_bytes_for(D, hkv, pl.hb);
+  s.max_ranges = max_ranges_for(qpk, hkv, sms, pl.fp16 != 0);
   const int threads = (pl.nw + 1) * 32;
   for (int target = target_ctas_per_sm(pl); target >= 1; --target) {
     const int fixed = smem_for(pl, D, 0, s.stage_bytes);
@@ -1533,7 +1914,7 @@ extern "C" size_t iris_b200_decode_workspace_bytes(int32_t batch, int32_t num_q_
       .bytes;
 }
 
-extern "C" int iris_b200_int4_paged_decode(const void* query, const void* k_data, const void* v_data,
+static int decode_entry(bool fp16, const void* query, const void* k_data, const void* v_data,
                                            const void* k_scale, const void* v_scale, const int32_t* block_table,
                                            int64_t block_table_stride, const int32_t* seq_lens, void* output,
                                            float* out_lse, int32_t out_mode, int32_t batch, int32_t num_q_heads,
@@ -1550,14 +1931,15 @@ extern "C" int iris_b200_int4_paged_decode(const void* query, const void* k_data
   if (out_mode != IRIS_DECODE_OUT_FP16 && out_mode != IRIS_DECODE_OUT_LSE) return IRIS_EINVAL;
   if (batch == 0) return IRIS_OK;
   if (max_pages_per_seq > 0 && block_table_stride < max_pages_per_seq) return IRIS_EINVAL;
-  const void* ptrs[] = {query, k_data, v_data, k_scale, v_scale, seq_lens, output, workspace, error_word};
+  const void* ptrs[] = {query, k_data, v_data, seq_lens, output, workspace, error_word};
   for (const void* q : ptrs)
     if (q == nullptr) return IRIS_EINVAL;
+  if (!fp16 && (k_scale == nullptr || v_scale == nullptr)) return IRIS_EINVAL;
   if (max_pages_per_seq > 0 && block_table == nullptr) return IRIS_EINVAL;
   if (out_mode == IRIS_DECODE_OUT_LSE && out_lse == nullptr) return IRIS_EINVAL;
   if (!(softmax_scale > 0.0f) && !(softmax_scale < 0.0f)) return IRIS_EINVAL;
   auto al = [](const void* q, uintptr_t a) { return reinterpret_cast<uintptr_t>(q) % a == 0; };
-  if (!al(k_data, 16) || !al(v_data, 16) || !al(k_scale, 16) || !al(v_scale, 16) || !al(query, 16) ||
+  if (!al(k_data, 16) || !al(v_data, 16) || (!fp16 && (!al(k_scale, 16) || !al(v_scale, 16))) || !al(query, 16) ||
       !al(output, 16) || !al(workspace, 256))
     return IRIS_EALIGN;
 
@@ -1567,14 +1949,15 @@ extern "C" int iris_b200_int4_paged_decode(const void* query, const void* k_data
     record_cuda_error(e0, "cudaGetDevice");
     return IRIS_ECUDA;
   }
-  const int32_t max_ranges = max_ranges_for(qpk, num_kv_heads, device_sms(device));
+  const int32_t max_ranges = max_ranges_for(qpk, num_kv_heads, device_sms(device), fp16);
   const Workspace ws = carve(workspace, batch, num_q_heads, head_dim, max_ranges);
   if (workspace_bytes < ws.bytes) return IRIS_EWORKSPACE;
 
   CUtensorMap km, vm;
-  const Plan plan = make_plan(head_dim, qpk, num_kv_heads);
-  if (!cached_kv_map(&km, k_data, head_dim, num_kv_heads, plan.hb, num_pages) ||
-      !cached_kv_map(&vm, v_data, head_dim, num_kv_heads, plan.hb, num_pages)) {
+  const Plan plan = fp16 ? make_plan_fp16(head_dim, qpk, num_kv_heads) : make_plan(head_dim, qpk, num_kv_heads);
+  const int fmt = fp16 ? 1 : 0;
+  if (!cached_kv_map(&km, fmt, k_data, head_dim, num_kv_heads, plan.hb, num_pages) ||
+      !cached_kv_map(&vm, fmt, v_data, head_dim, num_kv_heads, plan.hb, num_pages)) {
     snprintf(iris::g_last_error, sizeof(iris::g_last_error), "cuTensorMapEncodeTiled failed (D=%d Hkv=%d pages=%lld)", head_dim,
              num_kv_heads, static_cast<long long>(num_pages));
     return IRIS_ECUDA;
@@ -1610,6 +1993,41 @@ extern "C" int iris_b200_int4_paged_decode(const void* query, const void* k_data
   e = head_dim == 128 ? launch_decode<128>(plan, km, vm, p, device, s, max_ranges)
                       : launch_decode<64>(plan, km, vm, p, device, s, max_ranges);
   return e == cudaSuccess ? IRIS_OK : IRIS_ECUDA;
+}
+
+
+extern "C" int iris_b200_int4_paged_decode(const void* query, const void* k_data, const void* v_data,
+                                           const void* k_scale, const void* v_scale, const int32_t* block_table,
+                                           int64_t block_table_stride, const int32_t* seq_lens, void* output,
+                                           float* out_lse, int32_t out_mode, int32_t batch, int32_t num_q_heads,
+                                           int32_t num_kv_heads, int32_t head_dim, int64_t num_pages,
+                                           int32_t page_size, int32_t max_pages_per_seq, float softmax_scale,
+                                           void* workspace, size_t workspace_bytes, int32_t* error_word,
+                                           void* stream) {
+  return decode_entry(false, query, k_data, v_data, k_scale, v_scale, block_table, block_table_stride, seq_lens,
+                      output, out_lse, out_mode, batch, num_q_heads, num_kv_heads, head_dim, num_pages, page_size,
+                      max_pages_per_seq, softmax_scale, workspace, workspace_bytes, error_word, stream);
+}
+
+extern "C" size_t iris_b200_fp16_decode_workspace_bytes(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                                                        int32_t head_dim, int32_t device) {
+  if (batch <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || (head_dim != 64 && head_dim != 128)) return 0;
+  if (num_q_heads % num_kv_heads != 0) return 0;
+  return carve(nullptr, batch, num_q_heads, head_dim,
+               max_ranges_for(num_q_heads / num_kv_heads, num_kv_heads, device_sms(device), true))
+      .bytes;
+}
+
+extern "C" int iris_b200_fp16_paged_decode(const void* query, const void* k_cache, const void* v_cache,
+                                           const int32_t* block_table, int64_t block_table_stride,
+                                           const int32_t* seq_lens, void* output, float* out_lse, int32_t out_mode,
+                                           int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                                           int32_t head_dim, int64_t num_pages, int32_t page_size,
+                                           int32_t max_pages_per_seq, float softmax_scale, void* workspace,
+                                           size_t workspace_bytes, int32_t* error_word, void* stream) {
+  return decode_entry(true, query, k_cache, v_cache, nullptr, nullptr, block_table, block_table_stride, seq_lens,
+                      output, out_lse, out_mode, batch, num_q_heads, num_kv_heads, head_dim, num_pages, page_size,
+                      max_pages_per_seq, softmax_scale, workspace, workspace_bytes, error_word, stream);
 }
 
 namespace {

@@ -216,3 +216,68 @@ def merge_lse_packed(parts: torch.Tensor, num_parts: int, batch: int, num_q_head
                                                 _runtime.stream_ptr(parts.device)),
             "iris_b200_merge_lse_packed")
     return output
+
+
+def fused_fp16_paged_decode_attention(
+    query: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    block_table: torch.Tensor,
+    seq_lens: torch.Tensor,
+    output: torch.Tensor | None = None,
+    *,
+    page_size: int = 16,
+    softmax_scale: float | None = None,
+) -> torch.Tensor:
+    """Matched FP16 paged decode-attention baseline (reference
+    fused_attention.py:528-582: same signature, checks and exception types)
+    over ``k_cache / v_cache [pages, 16, Hkv, D]`` fp16, with the INT4
+    decode's schedule; semantics of torch_eager_fp16_paged_decode_attention."""
+    if k_cache.ndim != 4 or tuple(v_cache.shape) != tuple(k_cache.shape):
+        raise ValueError("k_cache/v_cache must have identical rank-4 shapes")
+    num_pages, cache_page_size, num_kv_heads, cache_dim = k_cache.shape
+    _, _, head_dim = query.shape
+    if cache_page_size != page_size or cache_dim != head_dim:
+        raise ValueError("FP16 cache shape does not match query/page_size")
+    _validate_common_decode_inputs(query, block_table, seq_lens, num_pages=num_pages, num_kv_heads=num_kv_heads,
+                                   page_size=page_size)
+    if k_cache.dtype != torch.float16 or v_cache.dtype != torch.float16:
+        raise TypeError("k_cache/v_cache must use FP16")
+    if k_cache.device != query.device or v_cache.device != query.device:
+        raise ValueError("k_cache/v_cache must be on the query device")
+    if output is None:
+        output = torch.empty_like(query)
+    elif output.shape != query.shape or output.dtype != query.dtype:
+        raise ValueError("output must match query shape and dtype")
+    elif output.device != query.device:
+        raise ValueError("output must be on the same device as query")
+    for name, t in (("query", query), ("k_cache", k_cache), ("v_cache", v_cache), ("output", output)):
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    if num_pages == 0:
+        raise IndexError("block_table contains an invalid physical page id")
+    if query.shape[0] == 0:
+        return output
+    if block_table.stride(1) != 1 and block_table.shape[1] > 1:
+        raise ValueError("block_table rows must be contiguous")
+    device = query.device
+    batch, hq, _ = query.shape
+    scale = head_dim ** -0.5 if softmax_scale is None or softmax_scale == 0.0 else float(softmax_scale)
+    with torch.cuda.device(device):
+        stream = _runtime.stream_ptr(device)
+        word = _runtime.error_word(device)
+        if not seq_lens.is_contiguous():
+            seq_lens = seq_lens.contiguous()
+        ws_bytes = _lib.lib.iris_b200_fp16_decode_workspace_bytes(batch, hq, num_kv_heads, head_dim,
+                                                                   device.index or 0)
+        ws = _runtime.scratch(device, stream, "decode_fp16", ws_bytes)
+        _lib.check_status(
+            _lib.lib.iris_b200_fp16_paged_decode(
+                query.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_table.data_ptr(),
+                block_table.stride(0), seq_lens.data_ptr(), output.data_ptr(), None, _lib.DECODE_OUT_FP16, batch, hq,
+                num_kv_heads, head_dim, num_pages, page_size, block_table.shape[1], scale, ws.data_ptr(), ws.numel(),
+                word.data_ptr(), stream),
+            "iris_b200_fp16_paged_decode")
+        if _runtime.validation_mode() == "sync":
+            _runtime.raise_for_bits(_runtime.read_and_clear(word))
+    return output

@@ -227,6 +227,42 @@ APPEND_KEYS = ("key", "value", "positions", "slot_mapping", "cos_cache", "sin_ca
 DECODE_KEYS = ("query", "k_data", "v_data", "k_scale", "v_scale", "block_table", "seq_lens")
 
 # decode cases exercised against the reference's eager decode
+def decode_random_fp16(seed, B, Hq, Hkv, D, lens, *, spare_pages=3, garbage_tail=True):
+    """FP16 paged cache ~N(0,1) with a random page permutation and ragged
+    lengths; slots past a sequence's end in its last page hold NaN / Inf
+    when ``garbage_tail``."""
+    rng = np.random.default_rng(seed)
+    P = 16
+    lens = np.asarray(lens, np.int32)
+    npg = [int(math.ceil(int(L) / P)) for L in lens]
+    NP = sum(npg) + spare_pages
+    perm = rng.permutation(NP).astype(np.int32)
+    bt = np.full((B, max(npg)), -1, np.int32)
+    o = 0
+    for b in range(B):
+        bt[b, :npg[b]] = perm[o:o + npg[b]]
+        o += npg[b]
+    kc = _randn16(rng, (NP, P, Hkv, D))
+    vc = _randn16(rng, (NP, P, Hkv, D))
+    if garbage_tail:
+        for b in range(B):
+            L = int(lens[b])
+            if L % P:
+                last = bt[b, npg[b] - 1]
+                kc[last, L % P:] = np.float16(np.nan)
+                vc[last, L % P:] = np.float16(np.inf)
+    q = _randn16(rng, (B, Hq, D))
+    return dict(query=q, k_cache=kc, v_cache=vc, block_table=bt, seq_lens=lens, page_size=P)
+
+
+FP16_DECODE_KEYS = ("query", "k_cache", "v_cache", "block_table", "seq_lens")
+
+FP16_DECODE_SPECS = {
+    "gqa4_d128": dict(seed=31, B=3, Hq=32, Hkv=8, D=128, lens=[1, 17, 700]),
+    "mha_d64": dict(seed=32, B=4, Hq=8, Hkv=8, D=64, lens=[16, 15, 33, 300]),
+    "gqa16_d128": dict(seed=33, B=2, Hq=32, Hkv=2, D=128, lens=[64, 129]),
+}
+
 DECODE_SPECS = {
     "gqa4_d128": dict(seed=21, B=3, Hq=16, Hkv=4, D=128, lens=[1, 17, 200]),
     "mha_d64": dict(seed=22, B=4, Hq=4, Hkv=4, D=64, lens=[16, 15, 33, 300]),

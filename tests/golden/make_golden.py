@@ -36,7 +36,8 @@ def _sha(a: np.ndarray) -> str:
 
 def main(ref_root: str) -> None:
     sys.path.insert(0, os.path.join(ref_root, "src"))
-    from iris_kernel.torch_eager_attention import torch_eager_int4_paged_decode_attention
+    from iris_kernel.torch_eager_attention import (torch_eager_fp16_paged_decode_attention,
+                                                   torch_eager_int4_paged_decode_attention)
     from iris_kernel.torch_eager_kv import pack_int4, quantize_int4_groupwise, torch_eager_append
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
@@ -98,6 +99,14 @@ def main(ref_root: str) -> None:
     for name, spec in cases.DECODE_SPECS.items():
         dc = cases.decode_random(**spec)
         run_decode(f"decode.{name}", dc)
+
+    # the matched FP16 decode (its eager reference casts the result to fp16)
+    for name, spec in cases.FP16_DECODE_SPECS.items():
+        fc = cases.decode_random_fp16(**spec)
+        t = {k: _t(fc[k]) for k in cases.FP16_DECODE_KEYS}
+        o = torch_eager_fp16_paged_decode_attention(t["query"], t["k_cache"], t["v_cache"], t["block_table"],
+                                                    t["seq_lens"], page_size=fc["page_size"])
+        out[f"fp16_decode.{name}.out.output"] = o.numpy()
 
     path = os.path.join(_HERE, "golden.npz")
     np.savez_compressed(path, **out)

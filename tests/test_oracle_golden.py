@@ -161,6 +161,15 @@ def test_decode_cases_match_reference(golden, name):
     _assert_fp16_close(_decode16(c), golden[f"decode.{name}.out.output"])
 
 
+@pytest.mark.parametrize("name", sorted(cases.FP16_DECODE_SPECS))
+def test_fp16_decode_cases_match_reference(golden, name):
+    """The matched FP16 decode oracle against the reference's eager FP16
+    decode (torch_eager_attention.py:243-294), NaN/Inf tail slots included."""
+    c = cases.decode_random_fp16(**cases.FP16_DECODE_SPECS[name])
+    got = orc.decode_attention_fp16(*[c[k] for k in cases.FP16_DECODE_KEYS]).astype(np.float16)
+    _assert_fp16_close(got, golden[f"fp16_decode.{name}.out.output"])
+
+
 def test_merge_of_split_partials_equals_full():
     c = cases.decode_random(**cases.DECODE_SPECS["gqa4_d128"])
     full, _ = orc.decode_attention_lse(*[c[k] for k in cases.DECODE_KEYS])
