@@ -124,6 +124,25 @@ IRIS_API int iris_b200_rope_int4_paged_append(const void* key, const void* value
 IRIS_API int iris_b200_int4_quantize_pack(const void* x, void* packed, void* scales, int64_t rows, int32_t head_dim,
                                           void* stream);
 
+/*
+ * FP16 paged append (the unquantised baseline write path): RoPE over the
+ * first rotary_dim dims of K (fp16 rounding after every operation, the rest
+ * of K passed through) and V copied, into k_cache / v_cache
+ * [num_pages, page_size, num_kv_heads, head_dim] fp16.  Replaces the
+ * _rope_fp16_paged_append launch of fused_rope_fp16_append
+ * (fused_kv.py:153-297); bit-exact with the reference test's eager
+ * expectation (apply_rope, torch_eager_kv.py:6-49, then a scatter).
+ * rotary_dim even and <= head_dim; slot < 0 skips the token.  Run
+ * iris_b200_append_check first on the same stream and error word: a batch it
+ * rejects is not written (as for the INT4 append).
+ */
+IRIS_API int iris_b200_rope_fp16_paged_append(const void* key, const void* value, const int32_t* positions,
+                                              const int32_t* slot_mapping, const void* cos_cache,
+                                              const void* sin_cache, void* k_cache, void* v_cache, int64_t num_tokens,
+                                              int32_t num_kv_heads, int32_t head_dim, int32_t rotary_dim,
+                                              int64_t max_position, int64_t num_pages, int32_t page_size,
+                                              int32_t* error_word, void* stream);
+
 /* ======================================================================
  * READ PATH
  * ====================================================================== */

@@ -313,6 +313,96 @@ __global__ void __launch_bounds__(256) quantize_pack_kernel(const __half* __rest
   scales[g] = sc;
 }
 
+// FP16 paged append (the reference's fused_rope_fp16_append): RoPE over the
+// first rotary_dim dims of K with fp16 rounding after every operation, the
+// rest of K and all of V copied, into k_cache / v_cache [pages, 16, H, D]
+// fp16 (row of (slot, head) at (slot * H + head) * D).  VEC: one thread per
+// 8-dim chunk (D % 8 == 0, rotary_dim % 16 == 0); otherwise one per dim.
+struct Fp16AppendParams {
+  const __half* key;
+  const __half* value;
+  const int32_t* positions;
+  const int32_t* slots;
+  const __half* cos_cache;
+  const __half* sin_cache;
+  __half* k_cache;
+  __half* v_cache;
+  int64_t num_tokens;
+  int64_t max_position;
+  int64_t num_slots;
+  int32_t num_heads, head_dim, rotary_dim;
+  int32_t* err;
+};
+
+template <bool VEC>
+__global__ void __launch_bounds__(256) rope_fp16_append_kernel(const Fp16AppendParams p) {
+  constexpr int W = VEC ? 8 : 1;  // dims per thread
+  const int per_row = p.head_dim / W;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t row = idx / per_row;
+  if (row >= p.num_tokens * p.num_heads) return;
+  const int c = static_cast<int>(idx - row * per_row);
+  const int64_t tok = row / p.num_heads;
+  const int64_t h = row - tok * p.num_heads;
+  const int32_t slot = __ldg(p.slots + tok);
+  if (slot < 0) return;
+  const int32_t pos = __ldg(p.positions + tok);
+  {
+    int32_t bits = 0;
+    if (static_cast<int64_t>(slot) >= p.num_slots) bits |= IRIS_ERR_SLOT_RANGE;
+    if (pos < 0) bits |= IRIS_ERR_POS_NEGATIVE;
+    else if (static_cast<int64_t>(pos) >= p.max_position) bits |= IRIS_ERR_POS_RANGE;
+    if (bits) {
+      if (h == 0 && c == 0) set_error(p.err, bits);
+      return;
+    }
+  }
+  const int d0 = c * W;
+  const int half = p.rotary_dim / 2;
+  const __half* krow = p.key + row * p.head_dim;
+  const __half* vrow = p.value + row * p.head_dim;
+  const int64_t dst = (static_cast<int64_t>(slot) * p.num_heads + h) * p.head_dim + d0;
+  if constexpr (VEC) {
+    uint4 k = ldg_nc_v4(krow + d0);
+    const uint4 v = ldg_nc_v4(vrow + d0);
+    if (d0 < p.rotary_dim) {
+      const bool lo = d0 < half;
+      const int j = lo ? d0 : d0 - half;  // cos/sin column
+      const uint4 par = ldg_nc_v4(krow + (lo ? d0 + half : d0 - half));
+      const uint4 cs = ldg_nc_v4(p.cos_cache + static_cast<int64_t>(pos) * half + j);
+      const uint4 sn = ldg_nc_v4(p.sin_cache + static_cast<int64_t>(pos) * half + j);
+      __half2* own = reinterpret_cast<__half2*>(&k);
+      const __half2* pr = reinterpret_cast<const __half2*>(&par);
+      const __half2* cc = reinterpret_cast<const __half2*>(&cs);
+      const __half2* ss = reinterpret_cast<const __half2*>(&sn);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __half2 pi = lo ? __hneg2(pr[i]) : pr[i];
+        own[i] = __hadd2(__hmul2_rn(own[i], cc[i]), __hmul2_rn(pi, ss[i]));
+      }
+    }
+    grid_dependency_wait();  // the check kernel before this launch has finished
+    if (p.err != nullptr && (*p.err & kRejectBits) != 0) return;
+    *reinterpret_cast<uint4*>(p.k_cache + dst) = k;
+    *reinterpret_cast<uint4*>(p.v_cache + dst) = v;
+  } else {
+    __half k = krow[d0];
+    const __half v = vrow[d0];
+    if (d0 < p.rotary_dim) {
+      const bool lo = d0 < half;
+      const int j = lo ? d0 : d0 - half;
+      const __half par = krow[lo ? d0 + half : d0 - half];
+      const __half cs = p.cos_cache[static_cast<int64_t>(pos) * half + j];
+      const __half sn = p.sin_cache[static_cast<int64_t>(pos) * half + j];
+      k = __hadd(__hmul_rn(k, cs), __hmul_rn(lo ? __hneg(par) : par, sn));
+    }
+    grid_dependency_wait();
+    if (p.err != nullptr && (*p.err & kRejectBits) != 0) return;
+    p.k_cache[dst] = k;
+    p.v_cache[dst] = v;
+  }
+}
+
 template <int D>
 static cudaError_t launch_append(const AppendParams& p, cudaStream_t stream) {
   using C = AppendCfg<D>;
@@ -449,6 +539,63 @@ extern "C" int iris_b200_int4_quantize_pack(const void* x, void* packed, void* s
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     record_cuda_error(e, "quantize_pack_kernel launch");
+    return IRIS_ECUDA;
+  }
+  return IRIS_OK;
+}
+
+extern "C" int iris_b200_rope_fp16_paged_append(const void* key, const void* value, const int32_t* positions,
+                                                const int32_t* slot_mapping, const void* cos_cache,
+                                                const void* sin_cache, void* k_cache, void* v_cache,
+                                                int64_t num_tokens, int32_t num_kv_heads, int32_t head_dim,
+                                                int32_t rotary_dim, int64_t max_position, int64_t num_pages,
+                                                int32_t page_size, int32_t* error_word, void* stream) {
+  if (num_tokens < 0 || num_kv_heads <= 0 || head_dim <= 0 || page_size <= 0 || num_pages < 0) return IRIS_EINVAL;
+  if (rotary_dim < 0 || rotary_dim > head_dim || rotary_dim % 2 != 0) return IRIS_EINVAL;
+  if (num_tokens == 0) return IRIS_OK;
+  const void* ptrs[] = {key, value, positions, slot_mapping, k_cache, v_cache};
+  for (const void* q : ptrs)
+    if (q == nullptr) return IRIS_EINVAL;
+  if (rotary_dim > 0 && (cos_cache == nullptr || sin_cache == nullptr)) return IRIS_EINVAL;
+  Fp16AppendParams p;
+  p.key = static_cast<const __half*>(key);
+  p.value = static_cast<const __half*>(value);
+  p.positions = positions;
+  p.slots = slot_mapping;
+  p.cos_cache = static_cast<const __half*>(cos_cache);
+  p.sin_cache = static_cast<const __half*>(sin_cache);
+  p.k_cache = static_cast<__half*>(k_cache);
+  p.v_cache = static_cast<__half*>(v_cache);
+  p.num_tokens = num_tokens;
+  p.max_position = max_position;
+  p.num_slots = num_pages * page_size;
+  p.num_heads = num_kv_heads;
+  p.head_dim = head_dim;
+  p.rotary_dim = rotary_dim;
+  p.err = error_word;
+  const bool vec = head_dim % 8 == 0 && rotary_dim % 16 == 0 && aligned(key, 16) && aligned(value, 16) &&
+                   aligned(k_cache, 16) && aligned(v_cache, 16) && (rotary_dim == 0 || (aligned(cos_cache, 16) &&
+                                                                                        aligned(sin_cache, 16)));
+  const int64_t threads_total = num_tokens * num_kv_heads * (vec ? head_dim / 8 : head_dim);
+  const int threads = 256;
+  const int64_t blocks = (threads_total + threads - 1) / threads;
+  if (blocks > 0x7fffffffLL) return IRIS_EUNSUPPORTED;
+  clear_stale_cuda_error();
+  // programmatic launch: starts while the check kernel before it finishes
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = vec ? cudaLaunchKernelEx(&cfg, rope_fp16_append_kernel<true>, p)
+                            : cudaLaunchKernelEx(&cfg, rope_fp16_append_kernel<false>, p);
+  if (e != cudaSuccess) {
+    record_cuda_error(e, "rope_fp16_append_kernel launch");
     return IRIS_ECUDA;
   }
   return IRIS_OK;

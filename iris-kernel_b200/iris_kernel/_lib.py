@@ -54,6 +54,10 @@ SIGNATURES = {
     "iris_b200_merge_lse_partials": (ctypes.c_int, [_c_p, _c_p, _c_i32, _c_i64, _c_i32, _c_p, _c_p]),
     "iris_b200_merge_lse_packed": (ctypes.c_int, [_c_p, _c_i32, _c_i64, _c_i32, _c_p, _c_p]),
     "iris_b200_int4_quantize_pack": (ctypes.c_int, [_c_p, _c_p, _c_p, _c_i64, _c_i32, _c_p]),
+    "iris_b200_rope_fp16_paged_append": (
+        ctypes.c_int,
+        [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i32, _c_i32, _c_i64, _c_i64, _c_i32, _c_p,
+         _c_p]),
     "iris_b200_fp16_decode_workspace_bytes": (_c_sz, [_c_i32, _c_i32, _c_i32, _c_i32, _c_i32]),
     "iris_b200_fp16_paged_decode": (
         ctypes.c_int,

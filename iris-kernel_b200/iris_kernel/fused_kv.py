@@ -187,3 +187,101 @@ def fused_quantize_pack_int4(x: torch.Tensor, packed: torch.Tensor, scales: torc
             _lib.lib.iris_b200_int4_quantize_pack(x.data_ptr(), packed.data_ptr(), scales.data_ptr(), rows, head_dim,
                                                   _runtime.stream_ptr(x.device)),
             "iris_b200_int4_quantize_pack")
+
+
+def fused_rope_fp16_append(
+    key: torch.Tensor,
+    value: torch.Tensor,
+    positions: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    cos_cache: torch.Tensor,
+    sin_cache: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    *,
+    rotary_dim: int,
+    page_size: int,
+) -> None:
+    """FP16 paged append (reference fused_kv.py:153-297: same signature, checks
+    and exception types): RoPE(K) over ``rotary_dim`` dims with fp16 rounding
+    after every operation, K tail and V copied, into ``k_cache / v_cache
+    [pages, page_size, Hkv, D]`` fp16.  Validation runs on the device (no
+    host round trip before the write); a rejected batch writes nothing."""
+    if not torch.cuda.is_available():
+        raise RuntimeError("Iris fused kernels require CUDA")
+    if key.device.type != "cuda":
+        raise ValueError("key/value must be CUDA tensors")
+    if key.shape != value.shape:
+        raise ValueError("key and value must have identical shapes")
+    if key.ndim != 3:
+        raise ValueError("key/value must have shape [T, Hkv, D]")
+    if key.dtype != torch.float16:
+        raise TypeError("Stage A currently supports FP16 input")
+    if value.dtype != torch.float16:
+        raise TypeError("Stage A currently supports FP16 input")
+    num_tokens, num_kv_heads, head_dim = key.shape
+    if rotary_dim > head_dim:
+        raise ValueError("rotary_dim cannot exceed head_dim")
+    if rotary_dim % 2 != 0:
+        raise ValueError("rotary_dim must be even")
+    if page_size <= 0:
+        raise ValueError("page_size must be positive")
+    if positions.shape != (num_tokens,):
+        raise ValueError("positions must have shape [T]")
+    if slot_mapping.shape != (num_tokens,):
+        raise ValueError("slot_mapping must have shape [T]")
+    if tuple(k_cache.shape[1:]) != (page_size, num_kv_heads, head_dim):
+        raise ValueError("invalid k_cache shape")
+    if tuple(v_cache.shape) != tuple(k_cache.shape):
+        raise ValueError("k_cache and v_cache must have identical shapes")
+    if k_cache.dtype != torch.float16:
+        raise TypeError("Stage A cache must use FP16")
+    if v_cache.dtype != torch.float16:
+        raise TypeError("Stage A cache must use FP16")
+    device = key.device
+    for name, t in (("value", value), ("positions", positions), ("slot_mapping", slot_mapping),
+                    ("cos_cache", cos_cache), ("sin_cache", sin_cache), ("k_cache", k_cache), ("v_cache", v_cache)):
+        if t.device != device:
+            raise ValueError(f"{name} must be on {device}")
+    if positions.dtype != torch.int32:
+        raise TypeError("positions must use torch.int32")
+    if slot_mapping.dtype != torch.int32:
+        raise TypeError("slot_mapping must use torch.int32")
+    half = rotary_dim // 2
+    if cos_cache.ndim != 2:
+        raise ValueError("cos_cache must have shape [max_position, rotary_dim // 2]")
+    if sin_cache.shape != cos_cache.shape:
+        raise ValueError("sin_cache must match cos_cache")
+    if cos_cache.shape[-1] != half:
+        raise ValueError(f"RoPE cache width must be {half}")
+    if cos_cache.dtype != torch.float16:
+        raise TypeError("Stage A RoPE cache must use FP16")
+    if sin_cache.dtype != torch.float16:
+        raise TypeError("Stage A RoPE cache must use FP16")
+    for name, t in (("key", key), ("value", value), ("positions", positions), ("slot_mapping", slot_mapping),
+                    ("cos_cache", cos_cache), ("sin_cache", sin_cache), ("k_cache", k_cache), ("v_cache", v_cache)):
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    _runtime.require_sm100(device)
+    if num_tokens == 0:
+        return
+    num_pages = k_cache.shape[0]
+    with torch.cuda.device(device):
+        stream = _runtime.stream_ptr(device)
+        word = _runtime.error_word(device)
+        ws_bytes = _lib.lib.iris_b200_append_check_workspace_bytes(num_pages, page_size)
+        ws = _runtime.scratch(device, stream, "append_check", max(ws_bytes, 4))
+        _lib.check_status(
+            _lib.lib.iris_b200_append_check(positions.data_ptr(), slot_mapping.data_ptr(), num_tokens,
+                                            cos_cache.shape[0], num_pages, page_size, ws.data_ptr(), ws.numel(),
+                                            word.data_ptr(), stream),
+            "iris_b200_append_check")
+        _lib.check_status(
+            _lib.lib.iris_b200_rope_fp16_paged_append(
+                key.data_ptr(), value.data_ptr(), positions.data_ptr(), slot_mapping.data_ptr(),
+                cos_cache.data_ptr(), sin_cache.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), num_tokens,
+                num_kv_heads, head_dim, rotary_dim, cos_cache.shape[0], num_pages, page_size, word.data_ptr(),
+                stream),
+            "iris_b200_rope_fp16_paged_append")
+        if _runtime.validation_mode() == "sync":
+            _runtime.raise_for_bits(_runtime.read_and_clear(word))

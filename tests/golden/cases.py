@@ -257,6 +257,35 @@ def decode_random_fp16(seed, B, Hq, Hkv, D, lens, *, spare_pages=3, garbage_tail
 
 FP16_DECODE_KEYS = ("query", "k_cache", "v_cache", "block_table", "seq_lens")
 
+FP16_APPEND_KEYS = ("key", "value", "positions", "slot_mapping", "cos_cache", "sin_cache", "k_cache", "v_cache")
+
+
+def fp16_append_case(seed, T=7, H=4, D=128, rotary_dim=128, P=16, NP=4, base=10000.0, slots=None):
+    """The reference test's FP16 append case shape (tests/test_correctness.py:
+    327-458): random K/V and caches, scattered / negative slots."""
+    rng = np.random.default_rng(seed)
+    key = _randn16(rng, (T, H, D))
+    value = _randn16(rng, (T, H, D))
+    if slots is None:
+        slots = rng.permutation(NP * P)[:T].astype(np.int32)
+        slots[T // 3] = -1
+    positions = rng.integers(0, 64, T).astype(np.int32)
+    half = rotary_dim // 2
+    inv = 1.0 / (base ** (np.arange(0, rotary_dim, 2, dtype=np.float32) / rotary_dim))
+    freqs = np.arange(64, dtype=np.float32)[:, None] * inv[None, :]
+    return dict(key=key, value=value, positions=positions, slot_mapping=np.asarray(slots, np.int32),
+                cos_cache=np.cos(freqs).astype(np.float16), sin_cache=np.sin(freqs).astype(np.float16),
+                k_cache=_randn16(rng, (NP, P, H, D)), v_cache=_randn16(rng, (NP, P, H, D)),
+                rotary_dim=rotary_dim, page_size=P)
+
+
+FP16_APPEND_SPECS = {
+    "ref_shape": dict(seed=41),
+    "partial_rotary": dict(seed=42, D=128, rotary_dim=64),
+    "d64_many": dict(seed=43, T=40, H=2, D=64, rotary_dim=64, NP=8),
+    "odd_rotary": dict(seed=44, T=9, H=3, D=96, rotary_dim=36, NP=2),
+}
+
 FP16_DECODE_SPECS = {
     "gqa4_d128": dict(seed=31, B=3, Hq=32, Hkv=8, D=128, lens=[1, 17, 700]),
     "mha_d64": dict(seed=32, B=4, Hq=8, Hkv=8, D=64, lens=[16, 15, 33, 300]),

@@ -38,7 +38,7 @@ def main(ref_root: str) -> None:
     sys.path.insert(0, os.path.join(ref_root, "src"))
     from iris_kernel.torch_eager_attention import (torch_eager_fp16_paged_decode_attention,
                                                    torch_eager_int4_paged_decode_attention)
-    from iris_kernel.torch_eager_kv import pack_int4, quantize_int4_groupwise, torch_eager_append
+    from iris_kernel.torch_eager_kv import apply_rope, pack_int4, quantize_int4_groupwise, torch_eager_append
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     out: dict[str, np.ndarray] = {}
@@ -107,6 +107,21 @@ def main(ref_root: str) -> None:
         o = torch_eager_fp16_paged_decode_attention(t["query"], t["k_cache"], t["v_cache"], t["block_table"],
                                                     t["seq_lens"], page_size=fc["page_size"])
         out[f"fp16_decode.{name}.out.output"] = o.numpy()
+
+    # FP16 append: the reference test's expectation (apply_rope, then scatter)
+    for name, spec in cases.FP16_APPEND_SPECS.items():
+        c = cases.fp16_append_case(**spec)
+        t = {k: _t(c[k]) for k in cases.FP16_APPEND_KEYS}
+        valid = t["slot_mapping"] >= 0
+        slots = t["slot_mapping"][valid].long()
+        pos = t["positions"][valid].long()
+        half = c["rotary_dim"] // 2
+        rk = apply_rope(t["key"][valid], t["cos_cache"][pos][:, None, :half], t["sin_cache"][pos][:, None, :half],
+                        rotary_dim=c["rotary_dim"])
+        t["k_cache"][slots // c["page_size"], slots % c["page_size"]] = rk
+        t["v_cache"][slots // c["page_size"], slots % c["page_size"]] = t["value"][valid]
+        out[f"fp16_append.{name}.out.k_cache"] = t["k_cache"].numpy()
+        out[f"fp16_append.{name}.out.v_cache"] = t["v_cache"].numpy()
 
     path = os.path.join(_HERE, "golden.npz")
     np.savez_compressed(path, **out)

@@ -1,0 +1,61 @@
+"""The FP16 paged append (fused_rope_fp16_append) on the GPU: byte-exact
+against the reference test's expectation (golden fixtures) and the oracle,
+for full and partial rotary dims (vector and per-element kernels), a large
+batch, negative slots, and the reference's errors with the cache untouched."""
+import numpy as np
+import pytest
+import torch
+
+import cases
+from _refs import to_dev
+from oracle import iris_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def _fused(c):
+    from iris_kernel.fused_kv import fused_rope_fp16_append
+
+    t = to_dev(c, cases.FP16_APPEND_KEYS)
+    fused_rope_fp16_append(*[t[k] for k in cases.FP16_APPEND_KEYS], rotary_dim=c["rotary_dim"],
+                           page_size=c["page_size"])
+    torch.cuda.synchronize()
+    return t
+
+
+@pytest.mark.parametrize("name", sorted(cases.FP16_APPEND_SPECS))
+def test_matches_reference_bytes(golden, name):
+    c = cases.fp16_append_case(**cases.FP16_APPEND_SPECS[name])
+    t = _fused(c)
+    for k in ("k_cache", "v_cache"):
+        assert t[k].cpu().numpy().tobytes() == golden[f"fp16_append.{name}.out.{k}"].tobytes()
+
+
+def test_large_batch_matches_oracle():
+    c = cases.fp16_append_case(seed=45, T=4096, H=8, D=128, rotary_dim=128, NP=300)
+    t = _fused(c)
+    ref = {k: c[k].copy() for k in ("k_cache", "v_cache")}
+    orc.append_fp16(*[c[k] if k not in ref else ref[k] for k in cases.FP16_APPEND_KEYS],
+                    rotary_dim=c["rotary_dim"], page_size=c["page_size"])
+    for k in ("k_cache", "v_cache"):
+        assert t[k].cpu().numpy().tobytes() == ref[k].tobytes()
+
+
+def test_errors_leave_the_cache_untouched():
+    from iris_kernel.fused_kv import fused_rope_fp16_append
+
+    c = cases.fp16_append_case(seed=46)
+    for slots, exc in (([1, 2, 3, 3, -1, 5, 6], ValueError), ([1, 2, 3, 4, 5, 6, 64], IndexError)):
+        c2 = dict(c, slot_mapping=np.asarray(slots, np.int32))
+        t = to_dev(c2, cases.FP16_APPEND_KEYS)
+        before = {k: t[k].clone() for k in ("k_cache", "v_cache")}
+        with pytest.raises(exc):
+            fused_rope_fp16_append(*[t[k] for k in cases.FP16_APPEND_KEYS], rotary_dim=128, page_size=16)
+        for k in before:
+            assert torch.equal(t[k], before[k])
+    t = to_dev(c, cases.FP16_APPEND_KEYS)
+    with pytest.raises(ValueError):
+        fused_rope_fp16_append(*[t[k] for k in cases.FP16_APPEND_KEYS], rotary_dim=130, page_size=16)
+    with pytest.raises(TypeError):
+        fused_rope_fp16_append(*[t[k] for k in cases.FP16_APPEND_KEYS[:6]], t["k_cache"].float(),
+                               t["v_cache"].float(), rotary_dim=128, page_size=16)

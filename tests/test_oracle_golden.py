@@ -170,6 +170,16 @@ def test_fp16_decode_cases_match_reference(golden, name):
     _assert_fp16_close(got, golden[f"fp16_decode.{name}.out.output"])
 
 
+@pytest.mark.parametrize("name", sorted(cases.FP16_APPEND_SPECS))
+def test_fp16_append_matches_reference(golden, name):
+    """The FP16 append oracle against the reference test's own expectation
+    (its apply_rope, then the scatter), byte for byte."""
+    c = cases.fp16_append_case(**cases.FP16_APPEND_SPECS[name])
+    orc.append_fp16(*[c[k] for k in cases.FP16_APPEND_KEYS], rotary_dim=c["rotary_dim"], page_size=c["page_size"])
+    for k in ("k_cache", "v_cache"):
+        assert c[k].tobytes() == golden[f"fp16_append.{name}.out.{k}"].tobytes()
+
+
 def test_merge_of_split_partials_equals_full():
     c = cases.decode_random(**cases.DECODE_SPECS["gqa4_d128"])
     full, _ = orc.decode_attention_lse(*[c[k] for k in cases.DECODE_KEYS])
