@@ -1476,46 +1476,77 @@ __global__ void __maxnreg__(128) decode_fp16_kernel(const __grid_constant__ CUte
 }
 
 // ---------------------------------------------------------- combine kernel
-// One CTA of D/4 threads per (sequence, query head): merges the records of
-// every range the sequence touches.  Sequences finished inside one range
-// were written by the decode kernel and are skipped.
+// One CTA per sequence: merges, for every (query head, 4 dims) item, the
+// records of the ranges the sequence touches (record k: the first range's
+// record, then side 0 of each later range).  Records are read eight at a
+// time with an online rescale, so a typical sequence (a few ranges) costs one
+// round of loads.  Sequences finished inside one range were written by the
+// decode kernel and are skipped.
+constexpr int kCombineThreads = 1024;
+
 template <int D>
-__global__ void __launch_bounds__(D / 4) decode_combine_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const DecodeParams p) {
   grid_dependency_wait();  // records, prefix sums and (U, R) come from the decode kernel
-  const int b = blockIdx.x, qh = blockIdx.y, t = threadIdx.x;
+  const int b = blockIdx.x;
   const int64_t U = p.meta[0], R = p.meta[1];
   const int64_t ps = p.prefix[b], pe = p.prefix[b + 1];
   if (pe <= ps) return;
   const int64_t f = range_of_page(ps, U, R), l = range_of_page(pe - 1, U, R);
   if (f == l) return;
-  float mx = kNegInf;
-  for (int64_t r = f; r <= l; ++r) {
-    const int64_t rec = r * 2 + ((r == f && ps > range_start(r, U, R)) ? 1 : 0);
-    mx = fmaxf(mx, p.rec_lse[rec * p.hq + qh]);
-  }
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  float wsum = 0.f;
-  for (int64_t r = f; r <= l; ++r) {
-    const int64_t rec = r * 2 + ((r == f && ps > range_start(r, U, R)) ? 1 : 0);
-    const float w = ex2(p.rec_lse[rec * p.hq + qh] - mx);
-    const float4 o = *reinterpret_cast<const float4*>(p.rec_o + (rec * p.hq + qh) * D + 4 * t);
-    acc.x = fmaf(w, o.x, acc.x);
-    acc.y = fmaf(w, o.y, acc.y);
-    acc.z = fmaf(w, o.z, acc.z);
-    acc.w = fmaf(w, o.w, acc.w);
-    wsum += w;
-  }
-  const float inv = 1.0f / wsum;
-  const int64_t orow = static_cast<int64_t>(b) * p.hq + qh;
-  if (p.out_mode == IRIS_DECODE_OUT_FP16) {
-    uint2 u;
-    u.x = h2_as_u32(__floats2half2_rn(acc.x * inv, acc.y * inv));
-    u.y = h2_as_u32(__floats2half2_rn(acc.z * inv, acc.w * inv));
-    *reinterpret_cast<uint2*>(static_cast<__half*>(p.out) + orow * D + 4 * t) = u;
-  } else {
-    *reinterpret_cast<float4*>(static_cast<float*>(p.out) + orow * D + 4 * t) =
-        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-    if (t == 0) p.out_lse[orow] = mx + lg2(wsum);
+  const int n = static_cast<int>(l - f + 1);
+  const int64_t rec_first = f * 2 + (ps > range_start(f, U, R) ? 1 : 0);
+  constexpr int kQuads = D / 4;
+  for (int item = threadIdx.x; item < p.hq * kQuads; item += blockDim.x) {
+    const int qh = item / kQuads, t = item % kQuads;
+    float m = kNegInf, wsum = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k0 = 0; k0 < n; k0 += 8) {
+      float lse[8];
+      float4 o[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int k = k0 + i;
+        if (k < n) {
+          const int64_t rec = k == 0 ? rec_first : (f + k) * 2;
+          lse[i] = p.rec_lse[rec * p.hq + qh];
+          o[i] = *reinterpret_cast<const float4*>(p.rec_o + (rec * p.hq + qh) * D + 4 * t);
+        } else {
+          lse[i] = kNegInf;
+          o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+      float mc = m;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mc = fmaxf(mc, lse[i]);
+      const float c = ex2(m - mc);  // rescale of what was merged so far (0 on the first chunk)
+      acc.x *= c;
+      acc.y *= c;
+      acc.z *= c;
+      acc.w *= c;
+      wsum *= c;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float w = ex2(lse[i] - mc);  // 0 for padding
+        acc.x = fmaf(w, o[i].x, acc.x);
+        acc.y = fmaf(w, o[i].y, acc.y);
+        acc.z = fmaf(w, o[i].z, acc.z);
+        acc.w = fmaf(w, o[i].w, acc.w);
+        wsum += w;
+      }
+      m = mc;
+    }
+    const float inv = 1.0f / wsum;
+    const int64_t orow = static_cast<int64_t>(b) * p.hq + qh;
+    if (p.out_mode == IRIS_DECODE_OUT_FP16) {
+      uint2 u;
+      u.x = h2_as_u32(__floats2half2_rn(acc.x * inv, acc.y * inv));
+      u.y = h2_as_u32(__floats2half2_rn(acc.z * inv, acc.w * inv));
+      *reinterpret_cast<uint2*>(static_cast<__half*>(p.out) + orow * D + 4 * t) = u;
+    } else {
+      *reinterpret_cast<float4*>(static_cast<float*>(p.out) + orow * D + 4 * t) =
+          make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+      if (t == 0) p.out_lse[orow] = m + lg2(wsum);
+    }
   }
 }
 
@@ -1888,8 +1919,8 @@ cudaError_t launch_decode(const Plan& pl, const CUtensorMap& km, const CUtensorM
   }
   // programmatic launch: the combine CTAs are resident before the decode ends
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.batch, p.hq);
-  cfg.blockDim = dim3(D / 4);
+  cfg.gridDim = dim3(p.batch);
+  cfg.blockDim = dim3(kCombineThreads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
