@@ -15,6 +15,11 @@
 // absmax and scale need no communication and the 16 packed bytes leave in
 // one vector store.  The kernel is HBM-bound: per (token, head) it moves 4D
 // bytes in and D + D/8 bytes out.
+#include <cstdlib>
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "common.cuh"
 
 namespace iris {
@@ -55,7 +60,15 @@ struct AppendParams {
   FastDiv heads_div;  // row -> (token, head)
   FastDiv page_div;   // slot -> (page, offset)
   int32_t* err;
+  int64_t prefetch_rows;  // one-pass kernel: L2 prefetch distance in rows (0: none)
 };
+
+// 32-byte read-only load (sm_100 vector width), 32-byte aligned address.
+IRIS_DEV void ldg_nc_v8(const void* p, uint4& a, uint4& b) {
+  asm volatile("ld.global.nc.v8.u32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(a.x), "=r"(a.y), "=r"(a.z), "=r"(a.w), "=r"(b.x), "=r"(b.y), "=r"(b.z), "=r"(b.w)
+               : "l"(p));
+}
 
 IRIS_DEV uint4 ldg_nc_v4(const void* p) {
   uint4 r;
@@ -131,28 +144,29 @@ IRIS_DEV float rcp_approx(float x) {
 // Checked against the IEEE path on every exact tie and a dense sweep
 // (tests/test_gpu_append.py).
 //
-// 8 fp16 values (one 16-byte vector) -> 8 nibbles (one 32-bit word); `fast`
-// is false for a non-finite scale (IEEE path).
-IRIS_DEV uint32_t quant_pack_vec(const uint4& raw, float scale, float r, bool fast) {
+// 8 fp16 values (one 16-byte vector) -> 8 nibbles (one 32-bit word), for a
+// finite scale.
+IRIS_DEV uint32_t quant_pack_vec(const uint4& raw, float scale, float r) {
   const __half2* v = reinterpret_cast<const __half2*>(&raw);
-  if (!fast) {
-    const __half2 vv[4] = {v[0], v[1], v[2], v[3]};
-    return quant_pack8_ieee(vv, scale);
-  }
+  // the same operations on value pairs with the sm_100 packed fp32 forms
+  // (each lane rounds as its scalar counterpart does)
   const float kRound = 8388624.0f;  // 2^23 + 16
-  uint32_t word = 0;
+  const float2 r2 = make_float2(r, r), ns2 = make_float2(-scale, -scale), k2 = make_float2(kRound, kRound);
+  uint32_t b[8];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const float2 f = __half22float2(v[i]);
-    float y0 = __fmul_rn(f.x, r);
-    float y1 = __fmul_rn(f.y, r);
-    y0 = fmaf(fmaf(-y0, scale, f.x), r, y0);
-    y1 = fmaf(fmaf(-y1, scale, f.y), r, y1);
-    const uint32_t n0 = __float_as_uint(__fadd_rn(y0, kRound)) & 0xFu;
-    const uint32_t n1 = __float_as_uint(__fadd_rn(y1, kRound)) & 0xFu;
-    word |= (n0 | (n1 << 4)) << (8 * i);
+    float2 y = __fmul2_rn(f, r2);
+    y = __ffma2_rn(__ffma2_rn(y, ns2, f), r2, y);  // y + (f - y*scale) * r
+    const float2 z = __fadd2_rn(y, k2);
+    b[2 * i] = __float_as_uint(z.x);
+    b[2 * i + 1] = __float_as_uint(z.y);
   }
-  return word;
+  // byte i of the word = nibble(2i) | nibble(2i+1) << 4: gather the low bytes
+  // of the even and of the odd values, then merge the nibbles
+  const uint32_t ev = __byte_perm(__byte_perm(b[0], b[2], 0x0040), __byte_perm(b[4], b[6], 0x0040), 0x5410);
+  const uint32_t od = __byte_perm(__byte_perm(b[1], b[3], 0x0040), __byte_perm(b[5], b[7], 0x0040), 0x5410);
+  return (ev & 0x0F0F0F0Fu) | ((od << 4) & 0xF0F0F0F0u);
 }
 
 IRIS_DEV __half2 habs_max_vec(const uint4& raw) {
@@ -166,12 +180,21 @@ IRIS_DEV void quant_group(const uint4 (&g)[4], __half& scale16, uint4& packed) {
                           __hmax2_nan(habs_max_vec(g[2]), habs_max_vec(g[3])));
   scale16 = group_scale(__hmax_nan(__low2half(m), __high2half(m)));
   const float sc = __half2float(scale16);
-  const bool fast = fabsf(sc) <= 3.0e38f;  // finite: division-free path
-  const float r = rcp_approx(sc);
-  packed.x = quant_pack_vec(g[0], sc, r, fast);
-  packed.y = quant_pack_vec(g[1], sc, r, fast);
-  packed.z = quant_pack_vec(g[2], sc, r, fast);
-  packed.w = quant_pack_vec(g[3], sc, r, fast);
+  if (fabsf(sc) <= 3.0e38f) {  // finite: division-free path (one branch per group)
+    const float r = rcp_approx(sc);
+    packed.x = quant_pack_vec(g[0], sc, r);
+    packed.y = quant_pack_vec(g[1], sc, r);
+    packed.z = quant_pack_vec(g[2], sc, r);
+    packed.w = quant_pack_vec(g[3], sc, r);
+  } else {
+    const __half2* v = reinterpret_cast<const __half2*>(g);
+    const __half2 v0[4] = {v[0], v[1], v[2], v[3]}, v1[4] = {v[4], v[5], v[6], v[7]};
+    const __half2 v2[4] = {v[8], v[9], v[10], v[11]}, v3[4] = {v[12], v[13], v[14], v[15]};
+    packed.x = quant_pack8_ieee(v0, sc);
+    packed.y = quant_pack8_ieee(v1, sc);
+    packed.z = quant_pack8_ieee(v2, sc);
+    packed.w = quant_pack8_ieee(v3, sc);
+  }
 }
 
 // One thread owns one 32-dim quantisation group of one (token, kv-head) row,
@@ -189,13 +212,28 @@ struct AppendCfg {
 
 constexpr int32_t kRejectBits = IRIS_ERR_SLOT_RANGE | IRIS_ERR_POS_NEGATIVE | IRIS_ERR_POS_RANGE | IRIS_ERR_DUP_SLOT;
 
-template <int D>
+// kWide: the group's 64 bytes (and its cos / sin rows) arrive in two 32-byte
+// loads, so every sector a warp's load touches is used whole (with 16-byte
+// loads the lanes' 64-byte stride fetches each sector twice and the L1
+// throughput bounds the kernel).  Needs 32-byte aligned key / value / cos /
+// sin bases.
+template <int D, bool kWide>
 __global__ void __launch_bounds__(AppendCfg<D>::kThreads) rope_int4_append_kernel(const AppendParams p) {
   using C = AppendCfg<D>;
   const int tid = threadIdx.x;
   const int c = tid % C::kTpr;  // group within the row
   const uint32_t row = blockIdx.x * C::kRows + tid / C::kTpr;
   const uint32_t nrows = static_cast<uint32_t>(p.num_tokens) * static_cast<uint32_t>(p.num_heads);
+  if (tid == 0 && p.prefetch_rows > 0) {
+    // the K / V rows of the CTA about one resident wave later go to L2 now,
+    // so DRAM keeps streaming while this wave computes
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * C::kRows + p.prefetch_rows;
+    if (r0 < nrows) {
+      const int64_t n = nrows - r0 < C::kRows ? nrows - r0 : C::kRows;
+      prefetch_l2_bulk(p.key + r0 * D, static_cast<uint32_t>(n * D * 2));
+      prefetch_l2_bulk(p.value + r0 * D, static_cast<uint32_t>(n * D * 2));
+    }
+  }
   if (row >= nrows) return;  // no collective operations below
   const uint32_t tok = p.heads_div.div(row);
   const uint32_t h = row - tok * static_cast<uint32_t>(p.num_heads);
@@ -223,13 +261,24 @@ __global__ void __launch_bounds__(AppendCfg<D>::kThreads) rope_int4_append_kerne
   const __half* crow = p.cos_cache + static_cast<size_t>(pos) * (D / 2) + 32 * pair;
   const __half* srow = p.sin_cache + static_cast<size_t>(pos) * (D / 2) + 32 * pair;
   uint4 ko[4], kp[4], vo[4], cs[4], sn[4];
+  if constexpr (kWide) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    ko[i] = ldg_nc_v4(krow + 32 * c + 8 * i);
-    kp[i] = ldg_nc_v4(krow + 32 * partner + 8 * i);
-    vo[i] = ldg_nc_v4(vrow + 32 * c + 8 * i);
-    cs[i] = ldg_nc_v4(crow + 8 * i);
-    sn[i] = ldg_nc_v4(srow + 8 * i);
+    for (int i = 0; i < 4; i += 2) {
+      ldg_nc_v8(krow + 32 * c + 8 * i, ko[i], ko[i + 1]);
+      ldg_nc_v8(krow + 32 * partner + 8 * i, kp[i], kp[i + 1]);
+      ldg_nc_v8(vrow + 32 * c + 8 * i, vo[i], vo[i + 1]);
+      ldg_nc_v8(crow + 8 * i, cs[i], cs[i + 1]);
+      ldg_nc_v8(srow + 8 * i, sn[i], sn[i + 1]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      ko[i] = ldg_nc_v4(krow + 32 * c + 8 * i);
+      kp[i] = ldg_nc_v4(krow + 32 * partner + 8 * i);
+      vo[i] = ldg_nc_v4(vrow + 32 * c + 8 * i);
+      cs[i] = ldg_nc_v4(crow + 8 * i);
+      sn[i] = ldg_nc_v4(srow + 8 * i);
+    }
   }
 
   // ---- RoPE, fp16 rounding after each op ----
@@ -403,6 +452,46 @@ __global__ void __launch_bounds__(256) rope_fp16_append_kernel(const Fp16AppendP
   }
 }
 
+// L2 prefetch distance of the one-pass kernel in quarters of a resident wave
+// (IRIS_APPEND_PREFETCH=<quarters> overrides it, 0 turns it off; tuning).
+static int append_prefetch_quarters() {
+  static const int quarters = [] {
+    const char* e = getenv("IRIS_APPEND_PREFETCH");
+    return e != nullptr ? atoi(e) : 2;
+  }();
+  return quarters;
+}
+
+// IRIS_APPEND_WIDE=0 keeps the one-pass kernel on 16-byte loads (tuning).
+static bool append_wide_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("IRIS_APPEND_WIDE");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
+}
+
+// Resident CTAs per SM x SMs of a kernel, queried once per (kernel, device).
+static cudaError_t resident_ctas(const void* fn, int threads, int smem, int64_t* out) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int64_t> cache;
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(fn, device);
+  auto it = cache.find(key);
+  if (it == cache.end()) {
+    int n_sm = 0, n_occ = 0;
+    e = cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, device);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n_occ, fn, threads, smem);
+    if (e != cudaSuccess) return e;
+    it = cache.emplace(key, static_cast<int64_t>(n_sm) * n_occ).first;
+  }
+  *out = it->second;
+  return cudaSuccess;
+}
+
 template <int D>
 static cudaError_t launch_append(const AppendParams& p, cudaStream_t stream) {
   using C = AppendCfg<D>;
@@ -411,17 +500,30 @@ static cudaError_t launch_append(const AppendParams& p, cudaStream_t stream) {
   if (blocks == 0) return cudaSuccess;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
   // programmatic launch: starts while the check kernel before it finishes
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
-  cfg.blockDim = dim3(C::kThreads);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, rope_int4_append_kernel<D>, p);
+  const auto aligned32 = [](const void* a) { return (reinterpret_cast<uintptr_t>(a) & 31) == 0; };
+  const bool wide = aligned32(p.key) && aligned32(p.value) && aligned32(p.cos_cache) && aligned32(p.sin_cache) &&
+                    append_wide_enabled();
+  const auto fn = wide ? rope_int4_append_kernel<D, true> : rope_int4_append_kernel<D, false>;
+  AppendParams q = p;
+  q.prefetch_rows = 0;
+  const int quarters = append_prefetch_quarters();
+  if (quarters > 0) {
+    int64_t resident = 0;
+    const cudaError_t e = resident_ctas(reinterpret_cast<const void*>(fn), C::kThreads, 0, &resident);
+    if (e != cudaSuccess) return e;
+    q.prefetch_rows = quarters * resident / 4 * C::kRows;
+  }
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = 0;
+  return cudaLaunchKernelEx(&cfg, fn, q);
 }
 
 }  // namespace iris
@@ -484,7 +586,7 @@ extern "C" int iris_b200_rope_int4_paged_append(const void* key, const void* val
   if (!aligned(key, 16) || !aligned(value, 16) || !aligned(cos_cache, 16) || !aligned(sin_cache, 16) ||
       !aligned(k_data, 16) || !aligned(v_data, 16) || !aligned(k_scale, 2) || !aligned(v_scale, 2))
     return IRIS_EALIGN;
-  AppendParams p;
+  AppendParams p = {};
   p.key = static_cast<const __half*>(key);
   p.value = static_cast<const __half*>(value);
   p.positions = positions;

@@ -148,6 +148,12 @@ IRIS_DEV void tma_load_5d(void* dst, const CUtensorMap* map, int c0, int c1, int
 // async-proxy (TMA) accesses of the same bytes.
 IRIS_DEV void fence_proxy_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// Bulk prefetch of a global range into L2 (16-byte aligned, size a multiple of 16).
+IRIS_DEV void prefetch_l2_bulk(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+               : "memory");
+}
+
 IRIS_DEV void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -109,6 +109,53 @@ def test_config5a_decode_style_append_full():
     _assert_bytes_equal(_fused(c), _oracle(c))
 
 
+@pytest.mark.parametrize("H,D", [(3, 128), (1, 256), (8, 64), (5, 192), (2, 512)])
+def test_large_batches_all_rows_bit_exact(H, D):
+    """Batches of more than one resident wave of CTAs, so the L2 prefetch of
+    later CTAs' rows is active and runs past the end: odd head counts, a
+    ragged end, padding slots and random positions, every row compared with
+    the oracle."""
+    rng = np.random.default_rng(H * 1000 + D)
+    P = 16
+    T = -(-16500 // H) + 5  # rows >= 16384, not a multiple of the tile
+    NP = -(-T // P) + 8
+    x = rng.standard_normal((2, T, H, D), dtype=np.float32) * 2
+    x[rng.random(x.shape) < 0.01] *= 20
+    cos, sin = orc.rope_cache(4096, D, 10000.0)
+    slots = (rng.permutation(NP * P)[:T]).astype(np.int32)
+    slots[rng.random(T) < 0.03] = -1
+    c = dict(key=x[0].astype(np.float16), value=x[1].astype(np.float16),
+             positions=rng.integers(0, 4096, T).astype(np.int32), slot_mapping=slots, cos_cache=cos, sin_cache=sin,
+             k_data=np.full((NP, P, H, D // 2), 0x5A, np.uint8), v_data=np.full((NP, P, H, D // 2), 0x5A, np.uint8),
+             k_scale=np.full((NP, P, H, D // 32), 2.0, np.float16),
+             v_scale=np.full((NP, P, H, D // 32), 2.0, np.float16), rotary_dim=D, group_size=32, page_size=P)
+    _assert_bytes_equal(_fused(c), _oracle(c))
+
+
+def test_sixteen_byte_aligned_inputs_take_the_narrow_loads():
+    """K / V / cos / sin bases that are 16- but not 32-byte aligned use the
+    16-byte load form; the result is the same bytes."""
+    from iris_kernel.fused_kv import fused_rope_int4_paged_append
+
+    c = cases.append_outliers(seed=5, T=300, H=8, D=128, P=16, NP=32, max_pos=512)
+    ref = _oracle(c)
+    t = to_dev(c, cases.APPEND_KEYS)
+
+    def shifted(x):  # same values, base address 16 bytes past a 32-byte boundary
+        buf = torch.empty(x.numel() + 8, dtype=x.dtype, device=x.device)
+        y = buf[8:].view(x.shape)
+        y.copy_(x)
+        assert y.data_ptr() % 32 == 16
+        return y
+
+    for k in ("key", "value", "cos_cache", "sin_cache"):
+        t[k] = shifted(t[k])
+    fused_rope_int4_paged_append(*[t[k] for k in cases.APPEND_KEYS], rotary_dim=c["rotary_dim"],
+                                 group_size=c["group_size"], page_size=c["page_size"])
+    torch.cuda.synchronize()
+    _assert_bytes_equal({k: t[k].cpu().numpy() for k in CACHE}, ref)
+
+
 def test_config5b_prefill_append_full_size_sampled():
     """BASELINE config 5b at full size (8 x 8192 tokens, Hkv=8, D=128, fresh
     permuted pages): every written row must equal the oracle's; rows are
