@@ -93,6 +93,21 @@ def test_many_short_and_one_long_sequence():
     assert_decode_close(_fused(c), _oracle(c))
 
 
+def test_split_records_across_batch_shapes_on_one_workspace():
+    """Split-KV records live in the cached workspace, whose layout moves with
+    the batch shape: batches with different shapes and split patterns,
+    alternated on one stream and one workspace, keep giving the first
+    results."""
+    a = cases.decode_random(seed=81, B=3, Hq=32, Hkv=8, D=128, lens=[9000, 40, 5000])
+    b = cases.decode_random(seed=82, B=5, Hq=32, Hkv=8, D=128, lens=[700, 12000, 3, 3000, 2500])
+    first_a, first_b = _fused(a), _fused(b)
+    assert_decode_close(first_a, _oracle(a))
+    assert_decode_close(first_b, _oracle(b))
+    for _ in range(3):
+        assert torch.equal(_fused(a), first_a)
+        assert torch.equal(_fused(b), first_b)
+
+
 def test_softmax_scale_and_output_argument():
     from iris_kernel.fused_attention import fused_int4_paged_decode_attention
 

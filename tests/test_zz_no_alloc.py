@@ -34,7 +34,7 @@ def _regular(lib, t):
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     q = t["query"]
     ws_bytes = lib.iris_b200_decode_workspace_bytes(q.shape[0], q.shape[1], t["k_data"].shape[2], q.shape[2], 0)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    ws = torch.full((ws_bytes,), 0xA5, dtype=torch.uint8, device="cuda")  # contents do not matter
     head, errp, stream = _args(t, out, err)
     assert lib.iris_b200_int4_paged_decode(*head, ws.data_ptr(), ws.numel(), errp, stream) == 0
     torch.cuda.synchronize()
