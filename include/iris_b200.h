@@ -96,12 +96,17 @@ IRIS_API int iris_b200_append_check(const int32_t* positions, const int32_t* slo
  *   cos_cache, sin_cache [max_position, head_dim/2] fp16 (rotary_dim == head_dim)
  *   head_dim % 64 == 0, group size 32.
  * Slots / positions out of range are skipped and reported in *error_word
- * (may be NULL).  Duplicate slots are not detected here (use
- * iris_b200_append_check first, on the same stream and error word): when
- * *error_word already holds a slot, position or duplicate bit as the kernel
- * starts, the call writes nothing, so a batch the check rejected leaves the
- * cache untouched without a host round trip in between.
+ * (may be NULL).  Batches of more than IRIS_APPEND_INLINE_CHECK_TOKENS tokens
+ * are not checked for duplicate slots here (use iris_b200_append_check first,
+ * on the same stream and error word): when *error_word already holds a slot,
+ * position or duplicate bit as the kernel starts, the call writes nothing, so
+ * a batch the check rejected leaves the cache untouched without a host round
+ * trip in between.  Batches of at most IRIS_APPEND_INLINE_CHECK_TOKENS tokens
+ * get the whole iris_b200_append_check validation inside this call (one
+ * launch; a batch it rejects is not written and its bits are recorded), so
+ * the separate check may be skipped for them.
  */
+#define IRIS_APPEND_INLINE_CHECK_TOKENS 128
 IRIS_API int iris_b200_rope_int4_paged_append(const void* key, const void* value, const int32_t* positions,
                                      const int32_t* slot_mapping, const void* cos_cache, const void* sin_cache,
                                      void* k_data, void* v_data, void* k_scale, void* v_scale, int64_t num_tokens,

@@ -63,6 +63,10 @@ struct AppendParams {
   int64_t prefetch_rows;  // one-pass kernel: L2 prefetch distance in rows (0: none)
 };
 
+// Batches of at most this many tokens are validated inside the append kernel
+// (ranges and duplicate slots, by every CTA), with no check kernel before it.
+constexpr int64_t kInlineCheckTokens = IRIS_APPEND_INLINE_CHECK_TOKENS;
+
 // 32-byte read-only load (sm_100 vector width), 32-byte aligned address.
 IRIS_DEV void ldg_nc_v8(const void* p, uint4& a, uint4& b) {
   asm volatile("ld.global.nc.v8.u32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
@@ -217,13 +221,85 @@ constexpr int32_t kRejectBits = IRIS_ERR_SLOT_RANGE | IRIS_ERR_POS_NEGATIVE | IR
 // loads the lanes' 64-byte stride fetches each sector twice and the L1
 // throughput bounds the kernel).  Needs 32-byte aligned key / value / cos /
 // sin bases.
-template <int D, bool kWide>
+//
+// kInline: the batch is small (at most kInlineCheckTokens tokens) and every
+// CTA validates all of it before storing, instead of a check kernel before
+// the launch.
+template <int D, bool kWide, bool kInline>
 __global__ void __launch_bounds__(AppendCfg<D>::kThreads) rope_int4_append_kernel(const AppendParams p) {
   using C = AppendCfg<D>;
   const int tid = threadIdx.x;
   const int c = tid % C::kTpr;  // group within the row
   const uint32_t row = blockIdx.x * C::kRows + tid / C::kTpr;
   const uint32_t nrows = static_cast<uint32_t>(p.num_tokens) * static_cast<uint32_t>(p.num_heads);
+  const bool in_range = row < nrows;
+  const uint32_t rr = in_range ? row : 0u;  // rows past the end read row 0 and store nothing
+  const uint32_t tok = p.heads_div.div(rr);
+  const uint32_t h = rr - tok * static_cast<uint32_t>(p.num_heads);
+  const int32_t slot = __ldg(p.slots + tok);
+  const int32_t pos = __ldg(p.positions + tok);
+
+  const bool lo_half = c < C::kHalf;
+  const int pair = lo_half ? c : c - C::kHalf;  // group index into cos/sin
+  const int partner = lo_half ? c + C::kHalf : c - C::kHalf;
+  const __half* krow = p.key + static_cast<size_t>(rr) * D;
+  const __half* vrow = p.value + static_cast<size_t>(rr) * D;
+  uint4 ko[4], kp[4], vo[4], cs[4], sn[4];
+  // K / V loads of one group (they depend on neither the slot nor the position)
+  const auto load_kv = [&](int i) {
+    if constexpr (kWide) {
+      ldg_nc_v8(krow + 32 * c + 8 * i, ko[i], ko[i + 1]);
+      ldg_nc_v8(krow + 32 * partner + 8 * i, kp[i], kp[i + 1]);
+      ldg_nc_v8(vrow + 32 * c + 8 * i, vo[i], vo[i + 1]);
+    } else {
+      ko[i] = ldg_nc_v4(krow + 32 * c + 8 * i);
+      kp[i] = ldg_nc_v4(krow + 32 * partner + 8 * i);
+      vo[i] = ldg_nc_v4(vrow + 32 * c + 8 * i);
+    }
+  };
+  constexpr int kStep = kWide ? 2 : 1;  // 16-byte vectors per load
+  if constexpr (kInline) {
+    // issued before the batch check, whose latency they then overlap
+#pragma unroll
+    for (int i = 0; i < 4; i += kStep) load_kv(i);
+  }
+
+  bool batch_bad = false;
+  if constexpr (kInline) {
+    // uniform: a small batch is checked by every CTA as append_check_kernel
+    // checks a large one (ranges, then each live slot counted against all
+    // slots, four per broadcast read), while the loads above are in flight
+    __shared__ __align__(16) int32_t s_slot[kInlineCheckTokens];
+    const int T = static_cast<int>(p.num_tokens);
+    const int T4 = (T + 3) & ~3;
+    int32_t bits = 0;
+    for (int i = tid; i < T4; i += C::kThreads) {
+      int32_t s = -1;
+      if (i < T) {
+        s = __ldg(p.slots + i);
+        if (s >= 0) {
+          const int32_t ps = __ldg(p.positions + i);
+          if (static_cast<int64_t>(s) >= p.num_slots) bits |= IRIS_ERR_SLOT_RANGE;
+          if (ps < 0) bits |= IRIS_ERR_POS_NEGATIVE;
+          else if (static_cast<int64_t>(ps) >= p.max_position) bits |= IRIS_ERR_POS_RANGE;
+        }
+      }
+      s_slot[i] = s;
+    }
+    __syncthreads();
+    for (int i = tid; i < T; i += C::kThreads) {
+      const int32_t s = s_slot[i];
+      if (s < 0 || static_cast<int64_t>(s) >= p.num_slots) continue;
+      int hits = 0;
+      for (int j = 0; j < T4; j += 4) {
+        const int4 v = *reinterpret_cast<const int4*>(s_slot + j);
+        hits += (v.x == s) + (v.y == s) + (v.z == s) + (v.w == s);
+      }
+      if (hits > 1) bits |= IRIS_ERR_DUP_SLOT;
+    }
+    if (blockIdx.x == 0 && bits) set_error(p.err, bits);
+    batch_bad = __syncthreads_or(bits != 0);
+  }
   if (tid == 0 && p.prefetch_rows > 0) {
     // the K / V rows of the CTA about one resident wave later go to L2 now,
     // so DRAM keeps streaming while this wave computes
@@ -234,13 +310,7 @@ __global__ void __launch_bounds__(AppendCfg<D>::kThreads) rope_int4_append_kerne
       prefetch_l2_bulk(p.value + r0 * D, static_cast<uint32_t>(n * D * 2));
     }
   }
-  if (row >= nrows) return;  // no collective operations below
-  const uint32_t tok = p.heads_div.div(row);
-  const uint32_t h = row - tok * static_cast<uint32_t>(p.num_heads);
-
-  const int32_t slot = __ldg(p.slots + tok);
-  if (slot < 0) return;
-  const int32_t pos = __ldg(p.positions + tok);
+  if (!in_range || slot < 0) return;  // no collective operations below
   {
     int32_t bits = 0;
     if (static_cast<int64_t>(slot) >= p.num_slots) bits |= IRIS_ERR_SLOT_RANGE;
@@ -251,31 +321,15 @@ __global__ void __launch_bounds__(AppendCfg<D>::kThreads) rope_int4_append_kerne
       return;
     }
   }
-
-  // ---- loads ----
-  const bool lo_half = c < C::kHalf;
-  const int pair = lo_half ? c : c - C::kHalf;  // group index into cos/sin
-  const int partner = lo_half ? c + C::kHalf : c - C::kHalf;
-  const __half* krow = p.key + static_cast<size_t>(row) * D;
-  const __half* vrow = p.value + static_cast<size_t>(row) * D;
   const __half* crow = p.cos_cache + static_cast<size_t>(pos) * (D / 2) + 32 * pair;
   const __half* srow = p.sin_cache + static_cast<size_t>(pos) * (D / 2) + 32 * pair;
-  uint4 ko[4], kp[4], vo[4], cs[4], sn[4];
-  if constexpr (kWide) {
 #pragma unroll
-    for (int i = 0; i < 4; i += 2) {
-      ldg_nc_v8(krow + 32 * c + 8 * i, ko[i], ko[i + 1]);
-      ldg_nc_v8(krow + 32 * partner + 8 * i, kp[i], kp[i + 1]);
-      ldg_nc_v8(vrow + 32 * c + 8 * i, vo[i], vo[i + 1]);
+  for (int i = 0; i < 4; i += kStep) {
+    if constexpr (!kInline) load_kv(i);
+    if constexpr (kWide) {
       ldg_nc_v8(crow + 8 * i, cs[i], cs[i + 1]);
       ldg_nc_v8(srow + 8 * i, sn[i], sn[i + 1]);
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      ko[i] = ldg_nc_v4(krow + 32 * c + 8 * i);
-      kp[i] = ldg_nc_v4(krow + 32 * partner + 8 * i);
-      vo[i] = ldg_nc_v4(vrow + 32 * c + 8 * i);
+    } else {
       cs[i] = ldg_nc_v4(crow + 8 * i);
       sn[i] = ldg_nc_v4(srow + 8 * i);
     }
@@ -310,7 +364,7 @@ __global__ void __launch_bounds__(AppendCfg<D>::kThreads) rope_int4_append_kerne
   // means the batch is rejected: nothing is written, as the reference raises
   // before it writes.
   grid_dependency_wait();
-  if (p.err != nullptr && (*p.err & kRejectBits) != 0) return;
+  if (batch_bad || (p.err != nullptr && (*p.err & kRejectBits) != 0)) return;
   const uint32_t page = p.page_div.div(static_cast<uint32_t>(slot));
   const uint32_t off = static_cast<uint32_t>(slot) - page * static_cast<uint32_t>(p.page_size);
   const size_t crow_idx = (static_cast<size_t>(page) * p.page_size + off) * p.num_heads + h;  // cache row
@@ -499,18 +553,21 @@ static cudaError_t launch_append(const AppendParams& p, cudaStream_t stream) {
   const int64_t blocks = (rows + C::kRows - 1) / C::kRows;
   if (blocks == 0) return cudaSuccess;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
-  // programmatic launch: starts while the check kernel before it finishes
+  // programmatic launch: starts while the check kernel before it finishes;
+  // a small batch checks itself and starts after its predecessor as usual
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.stream = stream;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = p.num_tokens <= kInlineCheckTokens ? 0 : 1;
   const auto aligned32 = [](const void* a) { return (reinterpret_cast<uintptr_t>(a) & 31) == 0; };
   const bool wide = aligned32(p.key) && aligned32(p.value) && aligned32(p.cos_cache) && aligned32(p.sin_cache) &&
                     append_wide_enabled();
-  const auto fn = wide ? rope_int4_append_kernel<D, true> : rope_int4_append_kernel<D, false>;
+  const bool small = p.num_tokens <= kInlineCheckTokens;
+  const auto fn = small ? (wide ? rope_int4_append_kernel<D, true, true> : rope_int4_append_kernel<D, false, true>)
+                        : (wide ? rope_int4_append_kernel<D, true, false> : rope_int4_append_kernel<D, false, false>);
   AppendParams q = p;
   q.prefetch_rows = 0;
   const int quarters = append_prefetch_quarters();

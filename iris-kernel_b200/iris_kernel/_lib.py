@@ -28,6 +28,7 @@ DECODE_OUT_FP16 = 0
 DECODE_OUT_LSE = 1
 
 DECODE_NOALLOC_SCRATCH_BYTES = 32 << 20  # IRIS_DECODE_NOALLOC_SCRATCH_BYTES
+APPEND_INLINE_CHECK_TOKENS = 128  # IRIS_APPEND_INLINE_CHECK_TOKENS
 
 _c_i32, _c_i64, _c_sz, _c_p, _c_f = ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_float
 

@@ -26,6 +26,19 @@ def test_header_declares_entry_points():
     assert len(names) == len(set(names))
 
 
+def test_python_constants_match_the_header():
+    from iris_kernel import _lib
+
+    src = open(HEADER).read()
+    consts = dict(re.findall(r"#define (IRIS_\w+) (0x[0-9a-fA-F]+|\d+)\b", src))
+    for name, value in consts.items():
+        short = name[len("IRIS_"):]
+        if hasattr(_lib, short):
+            assert getattr(_lib, short) == int(value, 0), name
+    assert _lib.APPEND_INLINE_CHECK_TOKENS == int(consts["IRIS_APPEND_INLINE_CHECK_TOKENS"])
+    assert _lib.ERR_DUP_SLOT == int(consts["IRIS_ERR_DUP_SLOT"], 0)
+
+
 def test_library_exports_every_declared_symbol():
     from iris_kernel import _lib
 

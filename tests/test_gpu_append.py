@@ -256,6 +256,70 @@ def test_errors_raise_reference_types_and_leave_cache_untouched(bad, exc):
         assert torch.equal(t[k], before[k])
 
 
+@pytest.mark.parametrize("T", [128, 129, 300])
+@pytest.mark.parametrize("bad,exc", [("dup", ValueError), ("slot", IndexError), ("pos_big", IndexError)])
+def test_errors_on_both_validation_paths(T, bad, exc):
+    """Batches of at most 128 tokens are validated inside the append kernel,
+    larger ones by the check kernel before it: the same errors either way,
+    with the offending tokens at the ends of the batch."""
+    from iris_kernel.fused_kv import fused_rope_int4_paged_append
+
+    NP = -(-T // 16) + 4
+    c = cases.append_outliers(seed=T, T=T, H=2, D=128, P=16, NP=NP, max_pos=512)
+    sm = c["slot_mapping"]
+    live = np.flatnonzero(sm >= 0)
+    first, last = int(live[0]), int(live[-1])
+    if bad == "dup":
+        sm[last] = sm[first]
+    elif bad == "slot":
+        sm[last] = NP * 16
+    else:
+        c["positions"][first] = 512
+    t = to_dev(c, cases.APPEND_KEYS)
+    before = {k: t[k].clone() for k in CACHE}
+    with pytest.raises(exc):
+        fused_rope_int4_paged_append(*[t[k] for k in cases.APPEND_KEYS], rotary_dim=128, page_size=16)
+    for k in CACHE:
+        assert torch.equal(t[k], before[k])
+
+
+def test_c_abi_check_then_append_on_a_small_batch():
+    """A C-ABI caller that runs iris_b200_append_check before a small batch
+    (which the append also validates itself) gets the same bytes and the
+    same rejection."""
+    from iris_kernel import _lib
+
+    lib = _lib.lib
+    for dup in (False, True):
+        c = _small_case()
+        if dup:
+            c["slot_mapping"] = np.array([17, 2, -1, 31, 17, 47, 63], np.int32)
+        t = to_dev(c, cases.APPEND_KEYS)
+        before = {k: t[k].clone() for k in CACHE}
+        err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        NP, P = t["k_data"].shape[0], t["k_data"].shape[1]
+        T, H, D = t["key"].shape
+        ws = torch.zeros(max(lib.iris_b200_append_check_workspace_bytes(NP, P), 4), dtype=torch.uint8, device="cuda")
+        stream = torch.cuda.current_stream().cuda_stream
+        pos, sl = t["positions"], t["slot_mapping"]
+        assert lib.iris_b200_append_check(pos.data_ptr(), sl.data_ptr(), T, t["cos_cache"].shape[0], NP, P,
+                                          ws.data_ptr(), ws.numel(), err.data_ptr(), stream) == 0
+        assert lib.iris_b200_rope_int4_paged_append(
+            t["key"].data_ptr(), t["value"].data_ptr(), pos.data_ptr(), sl.data_ptr(), t["cos_cache"].data_ptr(),
+            t["sin_cache"].data_ptr(), t["k_data"].data_ptr(), t["v_data"].data_ptr(), t["k_scale"].data_ptr(),
+            t["v_scale"].data_ptr(), T, H, D, t["cos_cache"].shape[0], NP, P, err.data_ptr(), stream) == 0
+        torch.cuda.synchronize()
+        if dup:
+            assert int(err.item()) == _lib.ERR_DUP_SLOT
+            for k in CACHE:
+                assert torch.equal(t[k], before[k])
+        else:
+            assert int(err.item()) == 0
+            ref = _oracle(c)
+            for k in CACHE:
+                assert t[k].cpu().numpy().tobytes() == ref[k].tobytes(), k
+
+
 def test_deferred_validation_records_and_rejects_the_batch():
     """Deferred mode: no host sync in the call; the bad batch is recorded and,
     as in the reference (which raises before writing), nothing of it is
