@@ -639,7 +639,7 @@ def main():
                           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                           "validation": "deferred, errors raised once per step; the two calls replayed from a "
                                         "CUDA graph captured once"},
-            "gpu_launches": 4 * args.steps,
+            "gpu_launches": 3 * args.steps,  # decode, combine, append (a 64-token batch validates itself)
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "traffic": traffic,
                          "kernel": "decode (decode + combine launches) timed alone from a CUDA graph"},
