@@ -61,6 +61,10 @@ SPEC_TBS = 8.0
 
 # BASELINE config 5b: prefill-style append, 8 sequences x 8192 new tokens,
 # Hkv=8, D=128, fresh permuted pages, 1% of entries x20, RoPE base 500000.
+# BASELINE config 5a: decode-style append, 2048 sequences x 1 token, Hkv 1, D 128, positions
+# ~U[0, 32768), RoPE base 500000, scattered pages
+A5_T, A5_MAXPOS = 2048, 32768
+A5_BYTES = A5_T * (4 * D + D + D // 8) + A5_T * 8 + A5_T * 2 * (D // 2) * 2
 PF_S, PF_L = 8, 8192
 PF_BYTES = PF_S * PF_L * HKV * (4 * D + D + D // 8) + PF_S * PF_L * 8 + PF_L * 2 * (D // 2) * 2
 
@@ -297,6 +301,27 @@ def build_prefill(dev, seed):
                 vs=torch.zeros(npages, P, HKV, D // G, dtype=torch.float16, device=dev))
 
 
+def build_c5a(dev, seed):
+    from oracle import iris_oracle as orc  # RoPE table builder only (host arrays)
+
+    g = torch.Generator(device=dev).manual_seed(seed)
+    k = torch.randn(A5_T, 1, D, generator=g, device=dev)
+    v = torch.randn(A5_T, 1, D, generator=g, device=dev)
+    k[torch.rand(k.shape, generator=g, device=dev) < 0.01] *= 20
+    v[torch.rand(v.shape, generator=g, device=dev) < 0.01] *= 20
+    npages = 2 * A5_T
+    pages = torch.randperm(npages, generator=g, device=dev)[:A5_T]
+    slots = (pages * P + torch.randint(0, P, (A5_T,), generator=g, device=dev)).int()
+    pos = torch.randint(0, A5_MAXPOS, (A5_T,), generator=g, device=dev).int()
+    cos_np, sin_np = orc.rope_cache(A5_MAXPOS, D, 500000.0)
+    return dict(k=k.half(), v=v.half(), pos=pos, slots=slots, cos=torch.from_numpy(cos_np).to(dev),
+                sin=torch.from_numpy(sin_np).to(dev),
+                kd=torch.zeros(npages, P, 1, D // 2, dtype=torch.uint8, device=dev),
+                vd=torch.zeros(npages, P, 1, D // 2, dtype=torch.uint8, device=dev),
+                ks=torch.zeros(npages, P, 1, D // G, dtype=torch.float16, device=dev),
+                vs=torch.zeros(npages, P, 1, D // G, dtype=torch.float16, device=dev))
+
+
 def step_prefill(x):
     from iris_kernel.fused_kv import fused_rope_int4_paged_append
 
@@ -481,6 +506,15 @@ def main():
     del g_pf, x
     ms_pf = max_over_ranks(ms_pf, dist, dev)
     pf_us = ms_pf / pf_steps * 1e3
+    # config 5a decode-style append (2048 x 1 token, Hkv 1; its own inputs)
+    x5 = build_c5a(dev, seed=55 + rank)
+    iris_kernel.set_validation_mode("deferred")
+    g_a5 = graph_of(lambda: step_prefill(x5), dev)
+    ms_a5 = timed(g_a5.replay, pf_steps, dev, dist, args.warmup)
+    iris_kernel.check_errors(dev)
+    iris_kernel.set_validation_mode("sync")
+    del g_a5, x5
+    a5_us = max_over_ranks(ms_a5, dist, dev) / pf_steps * 1e3
 
     # config 4: split-context decode over the ranks (one NCCL all-gather per step)
     from iris_kernel import parallel
@@ -614,6 +648,10 @@ def main():
                                "us": pf_us, "tbs": world * PF_BYTES / (pf_us * 1e-6) / 1e12,
                                "pct_of_measured": 100 * PF_BYTES / (pf_us * 1e-6) / 1e9 / _peak_gbs()[0],
                                "tokens_per_s": world * PF_S * PF_L / (pf_us * 1e-6), "bytes": PF_BYTES},
+            "config5a_append": {"config": "BASELINE config 5a: 2048 sequences x 1 token, Hkv 1, D 128, "
+                                          "positions ~U[0, 32768)",
+                                "us": a5_us, "tbs": world * A5_BYTES / (a5_us * 1e-6) / 1e12,
+                                "tokens_per_s": world * A5_T / (a5_us * 1e-6), "bytes": A5_BYTES},
             "config4_split_context": {
                 "config": "BASELINE config 4: 16 x 131072 tokens, Hq 64, Hkv 8, D 128, 8192-token splits dealt "
                           "over the ranks; each rank's cache holds only its splits",
