@@ -139,7 +139,9 @@ IRIS_API int iris_b200_int4_quantize_pack(const void* x, void* packed, void* sca
  * expectation (apply_rope, torch_eager_kv.py:6-49, then a scatter).
  * rotary_dim even and <= head_dim; slot < 0 skips the token.  Run
  * iris_b200_append_check first on the same stream and error word: a batch it
- * rejects is not written (as for the INT4 append).
+ * rejects is not written (as for the INT4 append).  As for the INT4 append,
+ * batches of at most IRIS_APPEND_INLINE_CHECK_TOKENS tokens are validated
+ * inside this call, and the separate check may be skipped for them.
  */
 IRIS_API int iris_b200_rope_fp16_paged_append(const void* key, const void* value, const int32_t* positions,
                                               const int32_t* slot_mapping, const void* cos_cache,

@@ -216,6 +216,46 @@ struct AppendCfg {
 
 constexpr int32_t kRejectBits = IRIS_ERR_SLOT_RANGE | IRIS_ERR_POS_NEGATIVE | IRIS_ERR_POS_RANGE | IRIS_ERR_DUP_SLOT;
 
+// Validation of a small batch (at most kInlineCheckTokens tokens) inside an
+// append kernel, done by every CTA as append_check_kernel does it for a large
+// one: ranges, then each live slot counted against all slots (16-byte
+// broadcast reads of a shared copy).  Every thread of the CTA calls it; it
+// returns whether the batch is rejected, and CTA 0 records the bits.
+template <int kThreads>
+IRIS_DEV bool inline_batch_check(const int32_t* __restrict__ slots, const int32_t* __restrict__ positions, int T,
+                                 int64_t num_slots, int64_t max_position, int32_t* err) {
+  __shared__ __align__(16) int32_t s_slot[kInlineCheckTokens];
+  const int tid = threadIdx.x;
+  const int T4 = (T + 3) & ~3;
+  int32_t bits = 0;
+  for (int i = tid; i < T4; i += kThreads) {
+    int32_t s = -1;
+    if (i < T) {
+      s = __ldg(slots + i);
+      if (s >= 0) {
+        const int32_t ps = __ldg(positions + i);
+        if (static_cast<int64_t>(s) >= num_slots) bits |= IRIS_ERR_SLOT_RANGE;
+        if (ps < 0) bits |= IRIS_ERR_POS_NEGATIVE;
+        else if (static_cast<int64_t>(ps) >= max_position) bits |= IRIS_ERR_POS_RANGE;
+      }
+    }
+    s_slot[i] = s;
+  }
+  __syncthreads();
+  for (int i = tid; i < T; i += kThreads) {
+    const int32_t s = s_slot[i];
+    if (s < 0 || static_cast<int64_t>(s) >= num_slots) continue;
+    int hits = 0;
+    for (int j = 0; j < T4; j += 4) {
+      const int4 v = *reinterpret_cast<const int4*>(s_slot + j);
+      hits += (v.x == s) + (v.y == s) + (v.z == s) + (v.w == s);
+    }
+    if (hits > 1) bits |= IRIS_ERR_DUP_SLOT;
+  }
+  if (blockIdx.x == 0 && bits) set_error(err, bits);
+  return __syncthreads_or(bits != 0);
+}
+
 // kWide: the group's 64 bytes (and its cos / sin rows) arrive in two 32-byte
 // loads, so every sector a warp's load touches is used whole (with 16-byte
 // loads the lanes' 64-byte stride fetches each sector twice and the L1
@@ -265,41 +305,9 @@ __global__ void __launch_bounds__(AppendCfg<D>::kThreads) rope_int4_append_kerne
   }
 
   bool batch_bad = false;
-  if constexpr (kInline) {
-    // uniform: a small batch is checked by every CTA as append_check_kernel
-    // checks a large one (ranges, then each live slot counted against all
-    // slots, four per broadcast read), while the loads above are in flight
-    __shared__ __align__(16) int32_t s_slot[kInlineCheckTokens];
-    const int T = static_cast<int>(p.num_tokens);
-    const int T4 = (T + 3) & ~3;
-    int32_t bits = 0;
-    for (int i = tid; i < T4; i += C::kThreads) {
-      int32_t s = -1;
-      if (i < T) {
-        s = __ldg(p.slots + i);
-        if (s >= 0) {
-          const int32_t ps = __ldg(p.positions + i);
-          if (static_cast<int64_t>(s) >= p.num_slots) bits |= IRIS_ERR_SLOT_RANGE;
-          if (ps < 0) bits |= IRIS_ERR_POS_NEGATIVE;
-          else if (static_cast<int64_t>(ps) >= p.max_position) bits |= IRIS_ERR_POS_RANGE;
-        }
-      }
-      s_slot[i] = s;
-    }
-    __syncthreads();
-    for (int i = tid; i < T; i += C::kThreads) {
-      const int32_t s = s_slot[i];
-      if (s < 0 || static_cast<int64_t>(s) >= p.num_slots) continue;
-      int hits = 0;
-      for (int j = 0; j < T4; j += 4) {
-        const int4 v = *reinterpret_cast<const int4*>(s_slot + j);
-        hits += (v.x == s) + (v.y == s) + (v.z == s) + (v.w == s);
-      }
-      if (hits > 1) bits |= IRIS_ERR_DUP_SLOT;
-    }
-    if (blockIdx.x == 0 && bits) set_error(p.err, bits);
-    batch_bad = __syncthreads_or(bits != 0);
-  }
+  if constexpr (kInline)  // while the loads above are in flight
+    batch_bad = inline_batch_check<C::kThreads>(p.slots, p.positions, static_cast<int>(p.num_tokens), p.num_slots,
+                                                p.max_position, p.err);
   if (tid == 0 && p.prefetch_rows > 0) {
     // the K / V rows of the CTA about one resident wave later go to L2 now,
     // so DRAM keeps streaming while this wave computes
@@ -437,12 +445,16 @@ struct Fp16AppendParams {
   int32_t* err;
 };
 
-template <bool VEC>
+template <bool VEC, bool kInline>
 __global__ void __launch_bounds__(256) rope_fp16_append_kernel(const Fp16AppendParams p) {
   constexpr int W = VEC ? 8 : 1;  // dims per thread
   const int per_row = p.head_dim / W;
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t row = idx / per_row;
+  bool batch_bad = false;
+  if constexpr (kInline)  // a small batch: every CTA validates it (no check kernel before the launch)
+    batch_bad = inline_batch_check<256>(p.slots, p.positions, static_cast<int>(p.num_tokens), p.num_slots,
+                                        p.max_position, p.err);
   if (row >= p.num_tokens * p.num_heads) return;
   const int c = static_cast<int>(idx - row * per_row);
   const int64_t tok = row / p.num_heads;
@@ -485,7 +497,7 @@ __global__ void __launch_bounds__(256) rope_fp16_append_kernel(const Fp16AppendP
       }
     }
     grid_dependency_wait();  // the check kernel before this launch has finished
-    if (p.err != nullptr && (*p.err & kRejectBits) != 0) return;
+    if (batch_bad || (p.err != nullptr && (*p.err & kRejectBits) != 0)) return;
     *reinterpret_cast<uint4*>(p.k_cache + dst) = k;
     *reinterpret_cast<uint4*>(p.v_cache + dst) = v;
   } else {
@@ -500,7 +512,7 @@ __global__ void __launch_bounds__(256) rope_fp16_append_kernel(const Fp16AppendP
       k = __hadd(__hmul_rn(k, cs), __hmul_rn(lo ? __hneg(par) : par, sn));
     }
     grid_dependency_wait();
-    if (p.err != nullptr && (*p.err & kRejectBits) != 0) return;
+    if (batch_bad || (p.err != nullptr && (*p.err & kRejectBits) != 0)) return;
     p.k_cache[dst] = k;
     p.v_cache[dst] = v;
   }
@@ -750,9 +762,13 @@ extern "C" int iris_b200_rope_fp16_paged_append(const void* key, const void* val
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  const cudaError_t e = vec ? cudaLaunchKernelEx(&cfg, rope_fp16_append_kernel<true>, p)
-                            : cudaLaunchKernelEx(&cfg, rope_fp16_append_kernel<false>, p);
+  const bool small = num_tokens <= kInlineCheckTokens;  // validated inside the kernel, ordinary launch
+  cfg.numAttrs = small ? 0 : 1;
+  const cudaError_t e =
+      small ? (vec ? cudaLaunchKernelEx(&cfg, rope_fp16_append_kernel<true, true>, p)
+                   : cudaLaunchKernelEx(&cfg, rope_fp16_append_kernel<false, true>, p))
+            : (vec ? cudaLaunchKernelEx(&cfg, rope_fp16_append_kernel<true, false>, p)
+                   : cudaLaunchKernelEx(&cfg, rope_fp16_append_kernel<false, false>, p));
   if (e != cudaSuccess) {
     record_cuda_error(e, "rope_fp16_append_kernel launch");
     return IRIS_ECUDA;

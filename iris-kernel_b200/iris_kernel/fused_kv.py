@@ -270,13 +270,14 @@ def fused_rope_fp16_append(
     with torch.cuda.device(device):
         stream = _runtime.stream_ptr(device)
         word = _runtime.error_word(device)
-        ws_bytes = _lib.lib.iris_b200_append_check_workspace_bytes(num_pages, page_size)
-        ws = _runtime.scratch(device, stream, "append_check", max(ws_bytes, 4))
-        _lib.check_status(
-            _lib.lib.iris_b200_append_check(positions.data_ptr(), slot_mapping.data_ptr(), num_tokens,
-                                            cos_cache.shape[0], num_pages, page_size, ws.data_ptr(), ws.numel(),
-                                            word.data_ptr(), stream),
-            "iris_b200_append_check")
+        if num_tokens > _lib.APPEND_INLINE_CHECK_TOKENS:  # smaller batches are checked by the append itself
+            ws_bytes = _lib.lib.iris_b200_append_check_workspace_bytes(num_pages, page_size)
+            ws = _runtime.scratch(device, stream, "append_check", max(ws_bytes, 4))
+            _lib.check_status(
+                _lib.lib.iris_b200_append_check(positions.data_ptr(), slot_mapping.data_ptr(), num_tokens,
+                                                cos_cache.shape[0], num_pages, page_size, ws.data_ptr(),
+                                                ws.numel(), word.data_ptr(), stream),
+                "iris_b200_append_check")
         _lib.check_status(
             _lib.lib.iris_b200_rope_fp16_paged_append(
                 key.data_ptr(), value.data_ptr(), positions.data_ptr(), slot_mapping.data_ptr(),

@@ -59,3 +59,30 @@ def test_errors_leave_the_cache_untouched():
     with pytest.raises(TypeError):
         fused_rope_fp16_append(*[t[k] for k in cases.FP16_APPEND_KEYS[:6]], t["k_cache"].float(),
                                t["v_cache"].float(), rotary_dim=128, page_size=16)
+
+
+@pytest.mark.parametrize("T", [64, 128, 129, 300])
+@pytest.mark.parametrize("bad,exc", [("dup", ValueError), ("slot", IndexError), ("pos", IndexError)])
+def test_errors_on_both_validation_paths(T, bad, exc):
+    """Batches of at most 128 tokens are validated inside the FP16 append,
+    larger ones by the check kernel before it: the same errors either way,
+    with the offending tokens at the ends of the batch."""
+    from iris_kernel.fused_kv import fused_rope_fp16_append
+
+    NP = -(-T // 16) + 4
+    c = cases.fp16_append_case(seed=T, T=T, H=2, D=128, rotary_dim=128, NP=NP)
+    sm = c["slot_mapping"]
+    live = np.flatnonzero(sm >= 0)
+    first, last = int(live[0]), int(live[-1])
+    if bad == "dup":
+        sm[last] = sm[first]
+    elif bad == "slot":
+        sm[last] = NP * 16
+    else:
+        c["positions"][first] = c["cos_cache"].shape[0]
+    t = to_dev(c, cases.FP16_APPEND_KEYS)
+    before = {k: t[k].clone() for k in ("k_cache", "v_cache")}
+    with pytest.raises(exc):
+        fused_rope_fp16_append(*[t[k] for k in cases.FP16_APPEND_KEYS], rotary_dim=128, page_size=16)
+    for k in before:
+        assert torch.equal(t[k], before[k])
