@@ -38,6 +38,18 @@ def set_validation_mode(mode: str) -> None:
     _state.mode = mode
 
 
+_cuda_seen = False
+
+
+def cuda_available() -> bool:
+    """``torch.cuda.is_available()``, remembered once it is true (the torch
+    call reads the environment and asks the driver on every call, ~5 us)."""
+    global _cuda_seen
+    if not _cuda_seen:
+        _cuda_seen = torch.cuda.is_available()
+    return _cuda_seen
+
+
 def validation_mode() -> str:
     return getattr(_state, "mode", "sync")
 
@@ -122,5 +134,27 @@ def scratch(device: torch.device, stream: int, kind: str, nbytes: int) -> torch.
     return buf
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_ptr(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    """The current torch CUDA stream of ``device`` as a raw handle (through
+    torch's raw-stream query when it has one: no Stream object per call)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if _raw_stream is not None:
+        return _raw_stream(idx)
+    return torch.cuda.current_stream(idx).cuda_stream
+
+
+_ws_sizes: dict = {}
+
+
+def workspace_bytes(fn, *shape) -> int:
+    """Workspace size from a library query, remembered per (query, shape)."""
+    key = (fn.__name__, shape)
+    n = _ws_sizes.get(key)
+    if n is None:
+        n = fn(*shape)
+        if len(_ws_sizes) < 4096:
+            _ws_sizes[key] = n
+    return n

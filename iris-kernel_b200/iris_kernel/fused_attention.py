@@ -20,7 +20,7 @@ def _validate_common_decode_inputs(query, block_table, seq_lens, *, num_pages, n
     """Host-side checks of fused_attention.py:373-434 minus the data-dependent
     ones (positive lengths, table length, page ids), which the kernels check
     on the device (see ``_runtime``)."""
-    if not torch.cuda.is_available():
+    if not _runtime.cuda_available():
         raise RuntimeError("Iris fused kernels require CUDA")
     if query.device.type != "cuda":
         raise ValueError("query must be a CUDA tensor")
@@ -96,7 +96,8 @@ def _launch(query, k_data, v_data, k_scale, v_scale, block_table, seq_lens, out,
         word = _runtime.error_word(device)
         if not seq_lens.is_contiguous():
             seq_lens = seq_lens.contiguous()
-        ws_bytes = _lib.lib.iris_b200_decode_workspace_bytes(batch, hq, hkv, head_dim, device.index or 0)
+        ws_bytes = _runtime.workspace_bytes(_lib.lib.iris_b200_decode_workspace_bytes, batch, hq, hkv, head_dim,
+                                            device.index or 0)
         ws = _runtime.scratch(device, stream, "decode", ws_bytes)
         _lib.check_status(
             _lib.lib.iris_b200_int4_paged_decode(
@@ -268,8 +269,8 @@ def fused_fp16_paged_decode_attention(
         word = _runtime.error_word(device)
         if not seq_lens.is_contiguous():
             seq_lens = seq_lens.contiguous()
-        ws_bytes = _lib.lib.iris_b200_fp16_decode_workspace_bytes(batch, hq, num_kv_heads, head_dim,
-                                                                   device.index or 0)
+        ws_bytes = _runtime.workspace_bytes(_lib.lib.iris_b200_fp16_decode_workspace_bytes, batch, hq,
+                                            num_kv_heads, head_dim, device.index or 0)
         ws = _runtime.scratch(device, stream, "decode_fp16", ws_bytes)
         _lib.check_status(
             _lib.lib.iris_b200_fp16_paged_decode(

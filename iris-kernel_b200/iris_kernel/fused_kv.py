@@ -112,7 +112,7 @@ def fused_rope_int4_paged_append(
     """RoPE(K), group-32 INT4 quantisation of K and V, low-nibble-first
     packing and paged append, in place.  Tokens with ``slot_mapping < 0`` are
     skipped; untouched slots stay byte-identical."""
-    if not torch.cuda.is_available():
+    if not _runtime.cuda_available():
         raise RuntimeError("Iris fused kernels require CUDA")
     num_tokens, num_kv_heads, head_dim, num_pages = _check_append_args(
         key, value, positions, slot_mapping, cos_cache, sin_cache, k_data, v_data, k_scale, v_scale,
@@ -151,7 +151,7 @@ def fused_quantize_pack_int4(x: torch.Tensor, packed: torch.Tensor, scales: torc
     in place.  Drop-in for fused_kv.py:362-416 of the reference (same checks,
     messages and exception types); bit-exact with its eager
     ``quantize_int4_groupwise`` + ``pack_int4``.  Tensors must be contiguous."""
-    if not torch.cuda.is_available():
+    if not _runtime.cuda_available():
         raise RuntimeError("Iris fused kernels require CUDA")
     if x.device.type != "cuda":
         raise ValueError("x must be a CUDA tensor")
@@ -208,7 +208,7 @@ def fused_rope_fp16_append(
     after every operation, K tail and V copied, into ``k_cache / v_cache
     [pages, page_size, Hkv, D]`` fp16.  Validation runs on the device (no
     host round trip before the write); a rejected batch writes nothing."""
-    if not torch.cuda.is_available():
+    if not _runtime.cuda_available():
         raise RuntimeError("Iris fused kernels require CUDA")
     if key.device.type != "cuda":
         raise ValueError("key/value must be CUDA tensors")
