@@ -59,6 +59,14 @@ extern "C" {
 /* Library version (major*10000 + minor*100 + patch). */
 IRIS_API int iris_b200_version(void);
 
+/*
+ * Self-test of the kernels' failure path: one thread waits, with the decode
+ * pipeline's bounded wait, on a barrier phase that nothing completes, gives
+ * up after limit_ns (0 < limit_ns <= 2e9) and ORs IRIS_ERR_PIPELINE_TIMEOUT
+ * into *error_word.  No fault, no hang; the context stays usable.
+ */
+IRIS_API int iris_b200_selftest_bounded_wait(int32_t* error_word, int64_t limit_ns, void* stream);
+
 /* Human-readable text for a status code. */
 IRIS_API const char* iris_b200_status_string(int status);
 

@@ -71,12 +71,12 @@ IRIS_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Returns false (and records the timeout) if the phase never completes.
-IRIS_DEV bool mbar_wait_bounded(uint32_t bar, uint32_t parity, int32_t* err) {
+IRIS_DEV bool mbar_wait_bounded(uint32_t bar, uint32_t parity, int32_t* err, uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+    if (globaltimer_ns() - t0 > limit_ns) break;
   }
   set_error(err, IRIS_ERR_PIPELINE_TIMEOUT);
   return false;

@@ -2096,6 +2096,34 @@ extern "C" int iris_b200_merge_lse_packed(const float* parts, int32_t num_parts,
 
 extern "C" const char* iris_b200_last_cuda_error(void) { return iris::g_last_error; }
 
+namespace {
+
+// One thread waits, through the decode pipeline's bounded wait, on an
+// mbarrier phase that nothing completes; after limit_ns it records the
+// timeout bit and returns.  Exercises the failure path without a fault.
+__global__ void bounded_wait_selftest_kernel(int32_t* err, uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x != 0) return;
+  iris::mbar_init(&bar, 1);
+  iris::fence_barrier_init();
+  iris::mbar_wait_bounded(iris::smem_u32(&bar), 0, err, limit_ns);  // phase 0 never completes
+}
+
+}  // namespace
+
+extern "C" int iris_b200_selftest_bounded_wait(int32_t* error_word, int64_t limit_ns, void* stream) {
+  if (error_word == nullptr || limit_ns <= 0 || limit_ns > 2000000000LL) return IRIS_EINVAL;
+  iris::clear_stale_cuda_error();
+  bounded_wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(error_word,
+                                                                               static_cast<uint64_t>(limit_ns));
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    iris::record_cuda_error(e, "bounded_wait_selftest_kernel launch");
+    return IRIS_ECUDA;
+  }
+  return IRIS_OK;
+}
+
 extern "C" int iris_b200_version(void) { return 100; }
 
 extern "C" const char* iris_b200_status_string(int status) {
