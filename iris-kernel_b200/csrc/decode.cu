@@ -1476,13 +1476,15 @@ __global__ void __maxnreg__(128) decode_fp16_kernel(const __grid_constant__ CUte
 }
 
 // ---------------------------------------------------------- combine kernel
-// One CTA per sequence: merges, for every (query head, 4 dims) item, the
-// records of the ranges the sequence touches (record k: the first range's
-// record, then side 0 of each later range).  Records are read eight at a
-// time with an online rescale, so a typical sequence (a few ranges) costs one
-// round of loads.  Sequences finished inside one range were written by the
-// decode kernel and are skipped.
-constexpr int kCombineThreads = 1024;
+// kCombineSplit CTAs per sequence, each a share of its (query head, 4 dims)
+// items (more SMs take part than with one CTA per sequence): an item merges
+// the records of the ranges the sequence touches (record k: the first
+// range's record, then side 0 of each later range).  Records are read eight
+// at a time with an online rescale, so a typical sequence (a few ranges)
+// costs one round of loads.  Sequences finished inside one range were written
+// by the decode kernel and are skipped.
+constexpr int kCombineThreads = 256;
+constexpr int kCombineSplit = 4;  // CTAs per sequence, each a quarter of its (query head, 4 dims) items
 
 template <int D>
 __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const DecodeParams p) {
@@ -1496,7 +1498,9 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const D
   const int n = static_cast<int>(l - f + 1);
   const int64_t rec_first = f * 2 + (ps > range_start(f, U, R) ? 1 : 0);
   constexpr int kQuads = D / 4;
-  for (int item = threadIdx.x; item < p.hq * kQuads; item += blockDim.x) {
+  const int items = p.hq * kQuads, per = (items + kCombineSplit - 1) / kCombineSplit;
+  const int i0 = blockIdx.y * per, i1 = min(items, i0 + per);
+  for (int item = i0 + threadIdx.x; item < i1; item += blockDim.x) {
     const int qh = item / kQuads, t = item % kQuads;
     float m = kNegInf, wsum = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -1919,7 +1923,7 @@ cudaError_t launch_decode(const Plan& pl, const CUtensorMap& km, const CUtensorM
   }
   // programmatic launch: the combine CTAs are resident before the decode ends
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.batch);
+  cfg.gridDim = dim3(p.batch, kCombineSplit);
   cfg.blockDim = dim3(kCombineThreads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
