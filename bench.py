@@ -425,6 +425,20 @@ def cpu_baseline_sample(seconds_budget=15.0):
                                     f"append), numpy oracle, {dt:.1f} s"), dt
 
 
+def _cpu_info():
+    """The host CPU the baseline ran on: model name and torch's intra-op thread count."""
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    model = ln.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"cpu_model": model, "torch_threads": torch.get_num_threads()}
+
+
 class _CpuSample:
     """The reference arm's CPU workload, built once: 4 of the config-2
     sequences (4096 tokens each, random cache contents) and their new tokens.
@@ -495,7 +509,8 @@ def run_reference(args, dist, rank, world):
         "ms_per_step": STEP_BYTES / (value * 1e12) * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "fp16/int4->fp32", "data": "synthetic",
         "config": _config(),
-        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": cores, "kind": "port", "sample": desc},
+        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": cores, "kind": "port", "sample": desc,
+                         **_cpu_info()},
         "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -679,7 +694,7 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, desc, _ = cpu_baseline_sample(seconds_budget=15.0)
-        cpu = {"value": v, "unit": "TB/s", "cores": os.cpu_count(), "kind": "port", "sample": desc}
+        cpu = {"value": v, "unit": "TB/s", "cores": os.cpu_count(), "kind": "port", "sample": desc, **_cpu_info()}
 
     if rank == 0:
         line = {
