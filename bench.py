@@ -1,101 +1,203 @@
 """Benchmark of the INT4 paged KV-cache hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--only all|c2|c3|c4|c5a|c5b|f16] [--no-cpu-baseline]
 
 Workload (Llama-3-8B shape): 64 sequences x 4096 tokens
 of INT4 paged cache (Hq=32, Hkv=8, D=128, page 16, group 32, pages scattered
-by a random permutation over a pool of 64 x 257 pages; K/V ~N(0,1) fp16 with
-4 outlier K channels x8, written by the fused append), then per step
+by a random permutation; K/V ~N(0,1) fp16 with 4 outlier K channels x8,
+written by the fused append), then per step
 
     decode attention over the 4096 cached tokens of every sequence, and
     a batched 1-token fused RoPE+INT4 append per sequence at position 4096.
 
-One process per GPU (torchrun for N > 1): every rank owns an independent
-copy of the workload (sequences are partitioned across GPUs, no collective),
-so ``scaling`` is "weak" and ``value`` is the aggregate over ranks.
+One process per GPU (torchrun for N > 1).  The 64 sequences are sharded
+64/N per GPU (sequence sharding: no collective), so the total work is fixed
+and ``scaling`` is "strong"; ``value`` is the whole batch's algorithmic bytes
+/ the max-over-ranks step time.
 
-``value``: algorithmic bytes of the step (decode + append) x N /
-max-over-ranks step time, in TB/s, with inputs resident in HBM; the step is
-replayed from a CUDA graph (validation in deferred mode, no host syncs).
+``value``: algorithmic bytes of the step (KV pages + scales read once, query
+read, output written, block table; append: fp16 K/V read, packed bytes and
+scales written, slots/positions and one RoPE row) / step time, in TB/s, with
+inputs resident in HBM; the step is replayed from a CUDA graph (validation in
+deferred mode, no host syncs).  Inputs (303 MB per step at N=1) exceed the
+126 MB L2, so no flush is needed between steps.
 ``e2e``: the same metric through the public Python API with host buffers:
 per step the new query / K / V / positions / slots are copied from pinned
 host memory, the decode and append calls run, the fp16 output is copied
-back, and any error the step's kernels recorded is raised (one host read per
-step, deferred validation mode).  ``e2e_sync`` is the same loop with every
-call reading the error word before it returns (the reference's per-call
-exceptions).
+back and the step's error word is read on the host.  The query copy comes
+first and the decode starts as soon as it lands; the K/V copy runs on a
+second stream meanwhile, and the output copy overlaps the append.
 
-Also reported: config 5b prefill append, config 4 split-context decode over
-the ranks (one NCCL all-gather per step), config 3 sequence-sharded decode.
+Also reported: config 5b prefill append, config 5a decode-style append,
+config 4 split-context decode over the ranks (one NCCL all-gather per step,
+with a per-stage breakdown and an FP32 parity self-check on two sequences),
+config 3 sequence-sharded decode, and the matched FP16 decode.
+
+``--impl reference`` times the reference's own CPU path (its torch eager
+``torch_eager_int4_paged_decode_attention`` + ``torch_eager_append``, from
+the unmodified install in ``baseline/_ref``) on the same workload, rank 0
+only, every step a measured step.
 """
 from __future__ import annotations
 
 import argparse
+import importlib.util
 import json
 import math
 import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "iris-kernel_b200"))
-sys.path.insert(0, ROOT)
 
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 B, L, HQ, HKV, D, P, G = 64, 4096, 32, 8, 128, 16, 32
-POOL = B * (L // P + 1)
 OUTLIER_CH = (3, 40, 77, 121)
-
-# algorithmic bytes (DESIGN.md "Measurement"): KV pages + scales read once,
-# Q read, O written, block table read; append reads K, V (fp16) and writes
-# packed bytes + scales, plus slots/positions and one cos/sin row.
-DECODE_BYTES = B * L * HKV * (D + D // 8) + 2 * B * HQ * D * 2 + B * (L // P + 1) * 4
-APPEND_BYTES = B * HKV * (4 * D + D + D // 8) + B * 8 + 2 * (D // 2) * 2
-STEP_BYTES = DECODE_BYTES + APPEND_BYTES
-FP16_BYTES = B * L * HKV * D * 2 * 2 + 2 * B * HQ * D * 2 + B * (L // P + 1) * 4
 SPEC_TBS = 8.0
 
-# BASELINE config 5b: prefill-style append, 8 sequences x 8192 new tokens,
-# Hkv=8, D=128, fresh permuted pages, 1% of entries x20, RoPE base 500000.
+
+def decode_bytes(nseq, ctx=L, hq=HQ, hkv=HKV, d=D):
+    """KV pages + scales read once, Q read, O written, block table read."""
+    return nseq * ctx * hkv * (d + d // 8) + 2 * nseq * hq * d * 2 + nseq * (ctx // P + 1) * 4
+
+
+def append_bytes(tokens, hkv=HKV, d=D, rope_rows=1):
+    """fp16 K and V read, packed bytes + scales written, slot + position, RoPE rows."""
+    return tokens * hkv * (4 * d + d + d // 8) + tokens * 8 + rope_rows * 2 * (d // 2) * 2
+
+
+DECODE_BYTES = decode_bytes(B)
+APPEND_BYTES = append_bytes(B)
+STEP_BYTES = DECODE_BYTES + APPEND_BYTES
+FP16_BYTES = B * L * HKV * D * 2 * 2 + 2 * B * HQ * D * 2 + B * (L // P + 1) * 4
+
 # BASELINE config 5a: decode-style append, 2048 sequences x 1 token, Hkv 1, D 128, positions
-# ~U[0, 32768), RoPE base 500000, scattered pages
+# ~U[0, 32768), RoPE base 500000, scattered pages.
 A5_T, A5_MAXPOS = 2048, 32768
 A5_BYTES = A5_T * (4 * D + D + D // 8) + A5_T * 8 + A5_T * 2 * (D // 2) * 2
+# BASELINE config 5b: prefill-style append, 8 sequences x 8192 new tokens, Hkv 8, D 128, fresh
+# permuted pages, 1% of entries x20, RoPE base 500000.
 PF_S, PF_L = 8, 8192
 PF_BYTES = PF_S * PF_L * HKV * (4 * D + D + D // 8) + PF_S * PF_L * 8 + PF_L * 2 * (D // 2) * 2
-
-
-# BASELINE config 4 (70B-shaped long context): 16 sequences x 131,072 tokens,
-# Hq 64, Hkv 8, D 128; split-context over the ranks in 8192-token splits,
-# every rank's cache holding only its splits; one NCCL all-gather + merge.
+# BASELINE config 4 (70B-shaped long context): 16 sequences x 131,072 tokens, Hq 64, Hkv 8, D 128;
+# split-context over the ranks in 8192-token splits, every rank's cache holding only its splits;
+# one NCCL all-gather + merge.
 C4_B, C4_L, C4_HQ, C4_HKV, C4_SPLIT = 16, 131072, 64, 8, 8192
 C4_BYTES = C4_B * C4_L * C4_HKV * (D + D // 8) + 2 * C4_B * C4_HQ * D * 2 + C4_B * (C4_L // P) * 4 + C4_B * 4
-# BASELINE config 3 (MHA, D 64, varlen): 128 sequences, Hq = Hkv = 16,
-# L ~ U[1, 16384] (seed 1); sequences sharded over the ranks by token count.
+C4_CHECK_SEQS = 2  # sequences the FP32 self-check covers
+# BASELINE config 3 (MHA, D 64, varlen): 128 sequences, Hq = Hkv = 16, L ~ U[1, 16384] (seed 1);
+# whole sequences sharded over the ranks by token count.
 C3_B, C3_H, C3_D, C3_LMAX = 128, 16, 64, 16384
 
 
-def _fill_cache(dev, g, kd, vd, ks, vs, slots, positions, hkv, d, cos, sin, chunk=65536):
-    """Write synthetic K/V ~ N(0, 0.5) through the fused append, in chunks."""
+def rope_tables(max_pos, dim, dev, base=10000.0):
+    """fp16 cos/sin tables [max_pos, dim/2] (NeoX rotation, angles in fp32)."""
+    inv = 1.0 / (base ** (torch.arange(0, dim, 2, dtype=torch.float32, device=dev) / dim))
+    f = torch.arange(max_pos, dtype=torch.float32, device=dev)[:, None] * inv[None, :]
+    return f.cos().half().contiguous(), f.sin().half().contiguous()
+
+
+def shard(world, rank, n=B):
+    """Sequences [lo, hi) of the config-2 batch that rank owns."""
+    return rank * n // world, (rank + 1) * n // world
+
+
+# ----------------------------------------------------------------- workloads
+
+def _fill_cache(dev, g, kd, vd, ks, vs, slots, positions, hkv, d, cos, sin, chunk=65536, std=0.5):
+    """Write synthetic K/V ~ N(0, std) through the fused append, in chunks."""
     from iris_kernel.fused_kv import fused_rope_int4_paged_append
 
     for t0 in range(0, slots.numel(), chunk):
         t1 = min(slots.numel(), t0 + chunk)
-        k = (torch.randn(t1 - t0, hkv, d, generator=g, device=dev) * 0.5).half()
-        v = (torch.randn(t1 - t0, hkv, d, generator=g, device=dev) * 0.5).half()
+        k = (torch.randn(t1 - t0, hkv, d, generator=g, device=dev) * std).half()
+        v = (torch.randn(t1 - t0, hkv, d, generator=g, device=dev) * std).half()
         fused_rope_int4_paged_append(k, v, positions[t0:t1].contiguous(), slots[t0:t1].contiguous(), cos, sin,
                                      kd, vd, ks, vs, rotary_dim=d, page_size=P)
+
+
+def build_c2(dev, seed, nseq):
+    """This rank's shard of config 2: nseq sequences of 4096 cached tokens
+    (257 pages each: the 1-token append at position 4096 needs one more)."""
+    from iris_kernel.fused_kv import fused_rope_int4_paged_append
+
+    g = torch.Generator(device=dev).manual_seed(seed)
+    pool = nseq * (L // P + 1)
+    bt = torch.randperm(pool, generator=g, device=dev).int().view(nseq, L // P + 1).contiguous()
+    kd = torch.zeros(pool, P, HKV, D // 2, dtype=torch.uint8, device=dev)
+    vd = torch.zeros_like(kd)
+    ks = torch.zeros(pool, P, HKV, D // G, dtype=torch.float16, device=dev)
+    vs = torch.zeros_like(ks)
+    cos, sin = rope_tables(L + 1, D, dev)
+    pos = torch.arange(L, device=dev, dtype=torch.int32)
+    for b in range(nseq):
+        k = torch.randn(L, HKV, D, generator=g, device=dev)
+        k[..., list(OUTLIER_CH)] *= 8
+        v = torch.randn(L, HKV, D, generator=g, device=dev)
+        slots = (bt[b, (pos // P).long()] * P + pos % P).int()
+        fused_rope_int4_paged_append(k.half(), v.half(), pos, slots, cos, sin, kd, vd, ks, vs, rotary_dim=D,
+                                     page_size=P)
+    q = torch.randn(nseq, HQ, D, generator=g, device=dev).half()
+    knew = torch.randn(nseq, HKV, D, generator=g, device=dev)
+    knew[..., list(OUTLIER_CH)] *= 8
+    vnew = torch.randn(nseq, HKV, D, generator=g, device=dev)
+    w = dict(q=q, kd=kd, vd=vd, ks=ks, vs=vs, bt=bt, cos=cos, sin=sin,
+             lens=torch.full((nseq,), L, dtype=torch.int32, device=dev),
+             knew=knew.half(), vnew=vnew.half(), newpos=torch.full((nseq,), L, dtype=torch.int32, device=dev),
+             newslot=(bt[:, L // P] * P).int().contiguous(),
+             out=torch.empty(nseq, HQ, D, dtype=torch.float16, device=dev))
+    torch.cuda.synchronize(dev)
+    return w
+
+
+def build_prefill(dev, seed):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    T = PF_S * PF_L
+    k = torch.randn(T, HKV, D, generator=g, device=dev)
+    v = torch.randn(T, HKV, D, generator=g, device=dev)
+    k[torch.rand(k.shape, generator=g, device=dev) < 0.01] *= 20
+    v[torch.rand(v.shape, generator=g, device=dev) < 0.01] *= 20
+    npages = T // P
+    pages = torch.randperm(npages, generator=g, device=dev).view(PF_S, PF_L // P)
+    pos = torch.arange(PF_L, device=dev, dtype=torch.int32).repeat(PF_S)
+    slots = (pages.repeat_interleave(P, dim=1) * P + torch.arange(PF_L, device=dev) % P).view(-1).int()
+    cos, sin = rope_tables(PF_L, D, dev, 500000.0)
+    return dict(k=k.half(), v=v.half(), pos=pos, slots=slots.contiguous(), cos=cos, sin=sin,
+                kd=torch.zeros(npages, P, HKV, D // 2, dtype=torch.uint8, device=dev),
+                vd=torch.zeros(npages, P, HKV, D // 2, dtype=torch.uint8, device=dev),
+                ks=torch.zeros(npages, P, HKV, D // G, dtype=torch.float16, device=dev),
+                vs=torch.zeros(npages, P, HKV, D // G, dtype=torch.float16, device=dev))
+
+
+def build_c5a(dev, seed):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    k = torch.randn(A5_T, 1, D, generator=g, device=dev)
+    v = torch.randn(A5_T, 1, D, generator=g, device=dev)
+    k[torch.rand(k.shape, generator=g, device=dev) < 0.01] *= 20
+    v[torch.rand(v.shape, generator=g, device=dev) < 0.01] *= 20
+    npages = 2 * A5_T
+    pages = torch.randperm(npages, generator=g, device=dev)[:A5_T]
+    slots = (pages * P + torch.randint(0, P, (A5_T,), generator=g, device=dev)).int()
+    pos = torch.randint(0, A5_MAXPOS, (A5_T,), generator=g, device=dev).int()
+    cos, sin = rope_tables(A5_MAXPOS, D, dev, 500000.0)
+    return dict(k=k.half(), v=v.half(), pos=pos, slots=slots, cos=cos, sin=sin,
+                kd=torch.zeros(npages, P, 1, D // 2, dtype=torch.uint8, device=dev),
+                vd=torch.zeros(npages, P, 1, D // 2, dtype=torch.uint8, device=dev),
+                ks=torch.zeros(npages, P, 1, D // G, dtype=torch.float16, device=dev),
+                vs=torch.zeros(npages, P, 1, D // G, dtype=torch.float16, device=dev))
 
 
 def build_c4(dev, rank, world, seed):
     """This rank's share of config 4: only the pages of its splits exist in
     its cache; the block table maps its split columns to them."""
     from iris_kernel import parallel
-    from oracle import iris_oracle as orc  # RoPE table builder only (host arrays)
 
     plan = parallel.plan_split_context([C4_L] * C4_B, world, rank, split_tokens=C4_SPLIT)
     g = torch.Generator(device=dev).manual_seed(seed)
@@ -118,8 +220,7 @@ def build_c4(dev, rank, world, seed):
     vd = torch.zeros_like(kd)
     ks = torch.zeros(n_local, P, C4_HKV, D // G, dtype=torch.float16, device=dev)
     vs = torch.zeros_like(ks)
-    cos_np, sin_np = orc.rope_cache(C4_L, D, 500000.0)
-    cos, sin = torch.from_numpy(cos_np).to(dev), torch.from_numpy(sin_np).to(dev)
+    cos, sin = rope_tables(C4_L, D, dev, 500000.0)
     _fill_cache(dev, g, kd, vd, ks, vs, torch.cat(slot_l), torch.cat(pos_l), C4_HKV, D, cos, sin)
     q = torch.randn(C4_B, C4_HQ, D, generator=torch.Generator(device=dev).manual_seed(4), device=dev).half()
     return dict(plan=plan, q=q, kd=kd, vd=vd, ks=ks, vs=vs, bt=bt)
@@ -128,7 +229,6 @@ def build_c4(dev, rank, world, seed):
 def build_c3(dev, rank, world, seed):
     """This rank's shard of config 3 (whole sequences, balanced by tokens)."""
     from iris_kernel import parallel
-    from oracle import iris_oracle as orc  # RoPE table builder only (host arrays)
 
     lens_all = np.random.default_rng(1).integers(1, C3_LMAX + 1, size=C3_B)
     mine = parallel.balance_sequences(lens_all, world)[rank]
@@ -152,9 +252,8 @@ def build_c3(dev, rank, world, seed):
     vd = torch.zeros_like(kd)
     ks = torch.zeros(pool, P, C3_H, C3_D // G, dtype=torch.float16, device=dev)
     vs = torch.zeros_like(ks)
-    cos_np, sin_np = orc.rope_cache(C3_LMAX, C3_D)
-    cos, sin = torch.from_numpy(cos_np).to(dev), torch.from_numpy(sin_np).to(dev)
-    _fill_cache(dev, g, kd, vd, ks, vs, torch.cat(slot_l), torch.cat(pos_l), C3_H, C3_D, cos, sin)
+    cos, sin = rope_tables(C3_LMAX, C3_D, dev)
+    _fill_cache(dev, g, kd, vd, ks, vs, torch.cat(slot_l), torch.cat(pos_l), C3_H, C3_D, cos, sin, std=1.0)
     q = torch.randn(len(mine), C3_H, C3_D, generator=g, device=dev).half()
     nbytes = int(lens.sum()) * C3_H * (C3_D + C3_D // 8) + 2 * len(mine) * C3_H * C3_D * 2 + int(npg.sum()) * 4
     total = int(lens_all.sum()) * C3_H * (C3_D + C3_D // 8) + 2 * C3_B * C3_H * C3_D * 2 + int(
@@ -164,12 +263,12 @@ def build_c3(dev, rank, world, seed):
                 out=torch.empty_like(q), bytes=nbytes, total_bytes=total)
 
 
+# ------------------------------------------------------------------ timing
+
 def _peak_gbs():
-    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
-        with open(path) as f:
-            v = float(json.load(f)["hbm_gbs"])
-        return v, "measured"
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
 
@@ -181,15 +280,19 @@ def _dist():
         import torch.distributed as dist
 
         local = int(os.environ.get("LOCAL_RANK", "0"))
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local))
+        else:
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
         return dist, dist.get_rank(), dist.get_world_size(), local
     return None, 0, 1, 0
 
 
 class Clocks:
-    """Samples SM clocks and throttle reasons with nvidia-smi while running."""
+    """Samples SM clocks and throttle reasons with nvidia-smi while running
+    (samples go to a temporary file)."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -198,18 +301,16 @@ class Clocks:
     def __init__(self, index):
         self.index = index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{index}.csv")
+        fd, self.path = tempfile.mkstemp(prefix=f"iris_clocks_{index}_", suffix=".csv")
+        os.close(fd)
 
     def __enter__(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
-            if os.path.exists(self.path):
-                os.remove(self.path)
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "50", "-f", self.path],
                                          stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
             t0 = time.time()  # start timing only once samples are flowing
-            while time.time() - t0 < 10 and (not os.path.exists(self.path) or os.path.getsize(self.path) == 0):
+            while time.time() - t0 < 10 and os.path.getsize(self.path) == 0:
                 time.sleep(0.05)
         except Exception:
             self.proc = None
@@ -228,118 +329,25 @@ class Clocks:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         rows = []
-        for line in open(self.path):
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
-            except ValueError:
-                continue
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+                except ValueError:
+                    continue
+        try:
+            os.remove(self.path)
+        except OSError:
+            pass
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v.lower() == "active"})
         return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
                 "power_w_max": max(r[2] for r in rows), "samples": len(rows), "reasons": reasons}
-
-
-def build_workload(dev, seed):
-    """Cache written by the fused append from synthetic K/V (config 2)."""
-    from iris_kernel.fused_kv import fused_rope_int4_paged_append
-    from oracle import iris_oracle as orc  # RoPE table builder only (host arrays)
-
-    g = torch.Generator(device=dev).manual_seed(seed)
-    perm = torch.randperm(POOL, generator=g, device=dev).int()
-    bt = perm.view(B, L // P + 1).contiguous()
-    kd = torch.zeros(POOL, P, HKV, D // 2, dtype=torch.uint8, device=dev)
-    vd = torch.zeros_like(kd)
-    ks = torch.zeros(POOL, P, HKV, D // G, dtype=torch.float16, device=dev)
-    vs = torch.zeros_like(ks)
-    cos_np, sin_np = orc.rope_cache(L + 1, D)
-    cos, sin = torch.from_numpy(cos_np).to(dev), torch.from_numpy(sin_np).to(dev)
-    pos = torch.arange(L, device=dev, dtype=torch.int32)
-    for b in range(B):
-        k = torch.randn(L, HKV, D, generator=g, device=dev)
-        k[..., list(OUTLIER_CH)] *= 8
-        v = torch.randn(L, HKV, D, generator=g, device=dev)
-        slots = (bt[b, (pos // P).long()] * P + pos % P).int()
-        fused_rope_int4_paged_append(k.half(), v.half(), pos, slots, cos, sin, kd, vd, ks, vs, rotary_dim=D,
-                                     page_size=P)
-    q = torch.randn(B, HQ, D, generator=g, device=dev).half()
-    knew = torch.randn(B, HKV, D, generator=g, device=dev)
-    knew[..., list(OUTLIER_CH)] *= 8
-    vnew = torch.randn(B, HKV, D, generator=g, device=dev)
-    w = dict(q=q, kd=kd, vd=vd, ks=ks, vs=vs, bt=bt, cos=cos, sin=sin,
-             lens=torch.full((B,), L, dtype=torch.int32, device=dev),
-             knew=knew.half(), vnew=vnew.half(), newpos=torch.full((B,), L, dtype=torch.int32, device=dev),
-             newslot=(bt[:, L // P] * P).int().contiguous(), out=torch.empty(B, HQ, D, dtype=torch.float16,
-                                                                             device=dev))
-    torch.cuda.synchronize(dev)
-    return w
-
-
-def build_prefill(dev, seed):
-    from oracle import iris_oracle as orc  # RoPE table builder only (host arrays)
-
-    g = torch.Generator(device=dev).manual_seed(seed)
-    T = PF_S * PF_L
-    k = torch.randn(T, HKV, D, generator=g, device=dev)
-    v = torch.randn(T, HKV, D, generator=g, device=dev)
-    k[torch.rand(k.shape, generator=g, device=dev) < 0.01] *= 20
-    v[torch.rand(v.shape, generator=g, device=dev) < 0.01] *= 20
-    npages = T // P
-    pages = torch.randperm(npages, generator=g, device=dev).view(PF_S, PF_L // P)
-    pos = torch.arange(PF_L, device=dev, dtype=torch.int32).repeat(PF_S)
-    slots = (pages.repeat_interleave(P, dim=1) * P + torch.arange(PF_L, device=dev) % P).view(-1).int()
-    cos_np, sin_np = orc.rope_cache(PF_L, D, 500000.0)
-    return dict(k=k.half(), v=v.half(), pos=pos, slots=slots.contiguous(), cos=torch.from_numpy(cos_np).to(dev),
-                sin=torch.from_numpy(sin_np).to(dev),
-                kd=torch.zeros(npages, P, HKV, D // 2, dtype=torch.uint8, device=dev),
-                vd=torch.zeros(npages, P, HKV, D // 2, dtype=torch.uint8, device=dev),
-                ks=torch.zeros(npages, P, HKV, D // G, dtype=torch.float16, device=dev),
-                vs=torch.zeros(npages, P, HKV, D // G, dtype=torch.float16, device=dev))
-
-
-def build_c5a(dev, seed):
-    from oracle import iris_oracle as orc  # RoPE table builder only (host arrays)
-
-    g = torch.Generator(device=dev).manual_seed(seed)
-    k = torch.randn(A5_T, 1, D, generator=g, device=dev)
-    v = torch.randn(A5_T, 1, D, generator=g, device=dev)
-    k[torch.rand(k.shape, generator=g, device=dev) < 0.01] *= 20
-    v[torch.rand(v.shape, generator=g, device=dev) < 0.01] *= 20
-    npages = 2 * A5_T
-    pages = torch.randperm(npages, generator=g, device=dev)[:A5_T]
-    slots = (pages * P + torch.randint(0, P, (A5_T,), generator=g, device=dev)).int()
-    pos = torch.randint(0, A5_MAXPOS, (A5_T,), generator=g, device=dev).int()
-    cos_np, sin_np = orc.rope_cache(A5_MAXPOS, D, 500000.0)
-    return dict(k=k.half(), v=v.half(), pos=pos, slots=slots, cos=torch.from_numpy(cos_np).to(dev),
-                sin=torch.from_numpy(sin_np).to(dev),
-                kd=torch.zeros(npages, P, 1, D // 2, dtype=torch.uint8, device=dev),
-                vd=torch.zeros(npages, P, 1, D // 2, dtype=torch.uint8, device=dev),
-                ks=torch.zeros(npages, P, 1, D // G, dtype=torch.float16, device=dev),
-                vs=torch.zeros(npages, P, 1, D // G, dtype=torch.float16, device=dev))
-
-
-def step_prefill(x):
-    from iris_kernel.fused_kv import fused_rope_int4_paged_append
-
-    fused_rope_int4_paged_append(x["k"], x["v"], x["pos"], x["slots"], x["cos"], x["sin"], x["kd"], x["vd"], x["ks"],
-                                 x["vs"], rotary_dim=D, page_size=P)
-
-
-def step_decode(w):
-    from iris_kernel.fused_attention import fused_int4_paged_decode_attention
-
-    fused_int4_paged_decode_attention(w["q"], w["kd"], w["vd"], w["ks"], w["vs"], w["bt"], w["lens"], w["out"])
-
-
-def step_append(w):
-    from iris_kernel.fused_kv import fused_rope_int4_paged_append
-
-    fused_rope_int4_paged_append(w["knew"], w["vnew"], w["newpos"], w["newslot"], w["cos"], w["sin"], w["kd"],
-                                 w["vd"], w["ks"], w["vs"], rotary_dim=D, page_size=P)
 
 
 def graph_of(fn, dev):
@@ -377,152 +385,288 @@ def timed(fn, steps, dev, dist, warmup):
     return st.elapsed_time(en)
 
 
-def max_over_ranks(x, dist, dev):
+def reduce_over_ranks(x, dist, dev, op="max"):
     if dist is None:
         return x
     t = torch.tensor([x], dtype=torch.float64, device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.MIN)
     return float(t.item())
 
 
-def cpu_baseline_sample(seconds_budget=15.0):
-    """The CPU oracle (numpy port of the reference's eager path) on a bounded
-    sample of the same workload: decode of whole 4096-token sequences plus the
-    64-token append, repeated until the budget is used.  Returns TB/s of
-    algorithmic bytes and a description."""
-    from oracle import iris_oracle as orc
+# ------------------------------------------------------- the reference's CPU path
 
-    rng = np.random.default_rng(0)
-    nseq = 4
-    NPs = nseq * (L // P)
-    kd = rng.integers(0, 256, (NPs, P, HKV, D // 2), dtype=np.uint8)
-    vd = rng.integers(0, 256, (NPs, P, HKV, D // 2), dtype=np.uint8)
-    ks = rng.uniform(0.01, 1, (NPs, P, HKV, D // G)).astype(np.float16)
-    vs = rng.uniform(0.01, 1, (NPs, P, HKV, D // G)).astype(np.float16)
-    bt = rng.permutation(NPs).astype(np.int32).reshape(nseq, L // P)
-    lens = np.full(nseq, L, np.int32)
-    q = rng.standard_normal((nseq, HQ, D)).astype(np.float16)
-    cos, sin = orc.rope_cache(L + 1, D)
-    knew = rng.standard_normal((B, HKV, D)).astype(np.float16)
-    vnew = rng.standard_normal((B, HKV, D)).astype(np.float16)
-    apool = B
-    akd = np.zeros((apool, P, HKV, D // 2), np.uint8)
-    avd, aks, avs = akd.copy(), np.zeros((apool, P, HKV, D // G), np.float16), None
-    avs = aks.copy()
-    done_bytes = 0
-    t0 = time.perf_counter()
-    reps = 0
-    while True:
-        orc.decode_attention(q, kd, vd, ks, vs, bt, lens)
-        orc.append(knew, vnew, np.full(B, L, np.int32), (np.arange(B) * P).astype(np.int32), cos, sin, akd, avd, aks,
-                   avs, rotary_dim=D, group_size=G, page_size=P)
-        reps += 1
-        done_bytes += nseq * L * HKV * (D + D // 8) + 2 * nseq * HQ * D * 2 + nseq * (L // P) * 4 + APPEND_BYTES
-        if time.perf_counter() - t0 > seconds_budget:
-            break
-    dt = time.perf_counter() - t0
-    return done_bytes / dt / 1e12, (f"{reps} x (decode of {nseq} of the 64 sequences x 4096 tokens + the 64-token "
-                                    f"append), numpy oracle, {dt:.1f} s"), dt
+def load_reference_eager():
+    """The reference's eager modules from the unmodified install in
+    baseline/_ref, loaded by file under private names (they import only
+    torch and math), or None when the install is absent."""
+    base = os.path.join(ROOT, "baseline", "_ref", "iris_kernel")
+    mods = {}
+    for name in ("torch_eager_attention", "torch_eager_kv"):
+        path = os.path.join(base, name + ".py")
+        if not os.path.isfile(path):
+            return None
+        spec = importlib.util.spec_from_file_location(f"_iris_reference_{name}", path)
+        m = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(m)
+        mods[name] = m
+    return mods
 
 
-def _cpu_info():
-    """The host CPU the baseline ran on: model name and torch's intra-op thread count."""
-    model = None
+def _host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def _cpu_model():
     try:
         with open("/proc/cpuinfo") as f:
             for ln in f:
                 if ln.startswith("model name"):
-                    model = ln.split(":", 1)[1].strip()
-                    break
+                    return ln.split(":", 1)[1].strip()
     except OSError:
         pass
-    return {"cpu_model": model, "torch_threads": torch.get_num_threads()}
+    return None
 
 
-class _CpuSample:
-    """The reference arm's CPU workload, built once: 4 of the config-2
-    sequences (4096 tokens each, random cache contents) and their new tokens.
-    A step is the numpy oracle's decode of one sequence over its first
-    `pages` pages plus the append of that sequence's new token."""
+class CpuStep:
+    """Config 2 on the host for the reference's eager code: the whole cache
+    (64 x 4096 tokens, random packed bytes and positive fp16 scales; the eager
+    code's cost does not depend on the values), queries, and the new tokens.
+    ``step(seqs)`` runs ``torch_eager_int4_paged_decode_attention`` over
+    sequences [0, seqs) and ``torch_eager_append`` of their new tokens, and
+    returns the algorithmic bytes it covered."""
 
-    def __init__(self, nseq=4):
-        from oracle import iris_oracle as orc
+    def __init__(self, ref):
+        self.dec = ref["torch_eager_attention"].torch_eager_int4_paged_decode_attention
+        self.app = ref["torch_eager_kv"].torch_eager_append
+        g = torch.Generator().manual_seed(0)
+        pool = B * (L // P + 1)
+        self.kd = torch.randint(0, 256, (pool, P, HKV, D // 2), dtype=torch.uint8, generator=g)
+        self.vd = torch.randint(0, 256, (pool, P, HKV, D // 2), dtype=torch.uint8, generator=g)
+        self.ks = (torch.rand((pool, P, HKV, D // G), generator=g) * 0.99 + 0.01).half()
+        self.vs = (torch.rand((pool, P, HKV, D // G), generator=g) * 0.99 + 0.01).half()
+        self.bt = torch.randperm(pool, generator=g).int().view(B, L // P + 1).contiguous()
+        self.lens = torch.full((B,), L, dtype=torch.int32)
+        self.q = torch.randn(B, HQ, D, generator=g).half()
+        self.knew = torch.randn(B, HKV, D, generator=g).half()
+        self.vnew = torch.randn(B, HKV, D, generator=g).half()
+        self.pos = torch.full((B,), L, dtype=torch.int32)
+        self.slot = (self.bt[:, L // P] * P).int().contiguous()
+        inv = 1.0 / (10000.0 ** (torch.arange(0, D, 2, dtype=torch.float32) / D))
+        f = torch.arange(L + 1, dtype=torch.float32)[:, None] * inv[None, :]
+        self.cos, self.sin = f.cos().half(), f.sin().half()
 
-        self.orc = orc
-        rng = np.random.default_rng(0)
-        self.nseq = nseq
-        NPs = nseq * (L // P)
-        self.kd = rng.integers(0, 256, (NPs, P, HKV, D // 2), dtype=np.uint8)
-        self.vd = rng.integers(0, 256, (NPs, P, HKV, D // 2), dtype=np.uint8)
-        self.ks = rng.uniform(0.01, 1, (NPs, P, HKV, D // G)).astype(np.float16)
-        self.vs = rng.uniform(0.01, 1, (NPs, P, HKV, D // G)).astype(np.float16)
-        self.bt = rng.permutation(NPs).astype(np.int32).reshape(nseq, L // P)
-        self.q = rng.standard_normal((nseq, HQ, D)).astype(np.float16)
-        self.cos, self.sin = orc.rope_cache(L + 1, D)
-        self.knew = rng.standard_normal((nseq, 1, HKV, D)).astype(np.float16)
-        self.vnew = rng.standard_normal((nseq, 1, HKV, D)).astype(np.float16)
-        self.akd = np.zeros((nseq, P, HKV, D // 2), np.uint8)
-        self.avd = self.akd.copy()
-        self.aks = np.zeros((nseq, P, HKV, D // G), np.float16)
-        self.avs = self.aks.copy()
-        self.i = 0
+    def step(self, seqs):
+        self.dec(self.q[:seqs], self.kd, self.vd, self.ks, self.vs, self.bt[:seqs], self.lens[:seqs],
+                 page_size=P, group_size=G)
+        self.app(self.knew[:seqs], self.vnew[:seqs], self.pos[:seqs], self.slot[:seqs], self.cos, self.sin,
+                 self.kd, self.vd, self.ks, self.vs, rotary_dim=D, group_size=G, page_size=P)
+        return decode_bytes(seqs) + append_bytes(seqs)
 
-    def step(self, pages):
-        """One step; returns its algorithmic bytes."""
-        b = self.i % self.nseq
-        self.i += 1
-        self.orc.decode_attention(self.q[b:b + 1], self.kd, self.vd, self.ks, self.vs, self.bt[b:b + 1],
-                                  np.array([pages * P], np.int32))
-        self.orc.append(self.knew[b], self.vnew[b], np.array([L], np.int32), np.array([b * P], np.int32), self.cos,
-                        self.sin, self.akd, self.avd, self.aks, self.avs, rotary_dim=D, group_size=G, page_size=P)
-        return pages * P * HKV * (D + D // 8) + 2 * HQ * D * 2 + pages * 4 + APPEND_BYTES // B
+
+def cpu_baseline_sample(seconds_budget=15.0):
+    """The reference's eager CPU path (or, without the install, the numpy
+    port of it) on a bounded sample of the workload: repeated steps over 4 of
+    the 64 sequences until the budget is used.  Returns the line's
+    cpu_baseline object."""
+    threads = _host_threads()
+    torch.set_num_threads(threads)
+    ref = load_reference_eager()
+    if ref is not None:
+        smp = CpuStep(ref)
+        smp.step(1)  # first touch
+        done, reps = 0, 0
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < seconds_budget:
+            done += smp.step(4)
+            reps += 1
+        dt = time.perf_counter() - t0
+        return {"value": done / dt / 1e12, "unit": "TB/s", "cores": threads, "kind": "reference",
+                "code": "torch_eager_int4_paged_decode_attention + torch_eager_append (baseline/_ref, unmodified)",
+                "sample": f"{reps} x (decode of 4 of the 64 config-2 sequences x 4096 tokens + their 1-token "
+                          f"appends), {dt:.1f} s", "cpu_model": _cpu_model(), "torch_threads": threads}
+    sys.path.insert(0, ROOT)
+    from oracle import iris_oracle as orc  # the numpy port, only when the reference is not installed
+
+    rng = np.random.default_rng(0)
+    nseq = 4
+    nps = nseq * (L // P)
+    kd = rng.integers(0, 256, (nps, P, HKV, D // 2), dtype=np.uint8)
+    vd = rng.integers(0, 256, (nps, P, HKV, D // 2), dtype=np.uint8)
+    ks = rng.uniform(0.01, 1, (nps, P, HKV, D // G)).astype(np.float16)
+    vs = rng.uniform(0.01, 1, (nps, P, HKV, D // G)).astype(np.float16)
+    bt = rng.permutation(nps).astype(np.int32).reshape(nseq, L // P)
+    q = rng.standard_normal((nseq, HQ, D)).astype(np.float16)
+    done, reps = 0, 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds_budget:
+        orc.decode_attention(q, kd, vd, ks, vs, bt, np.full(nseq, L, np.int32))
+        done += decode_bytes(nseq)
+        reps += 1
+    dt = time.perf_counter() - t0
+    return {"value": done / dt / 1e12, "unit": "TB/s", "cores": 1, "kind": "port",
+            "sample": f"{reps} x decode of 4 of the 64 config-2 sequences (numpy port; reference not installed), "
+                      f"{dt:.1f} s", "cpu_model": _cpu_model()}
 
 
 def run_reference(args, dist, rank, world):
-    """The reference's CPU path (numpy port of its eager code; the reference
-    itself does not travel to the GPU box) on host cores, rank 0 only.  Each
-    step decodes a chunk of one sequence, sized so that warm-up plus timed
-    steps take about 90 s whatever their number."""
+    """The reference's CPU path on the host cores, rank 0 only: every step
+    is a measured run of torch_eager_int4_paged_decode_attention over the
+    step's sequences plus torch_eager_append of their new tokens.  A step is
+    the full 64-sequence config-2 step unless warm-up + steps would then take
+    more than ~150 s; then every step covers the first n sequences (n sized
+    from a timed first step) and the line says so."""
     if rank != 0:
         return
-    smp = _CpuSample()
-    smp.step(L // P)  # first touch of the arrays
+    ref = load_reference_eager()
+    if ref is None:
+        print(json.dumps({"impl": "reference", "unavailable": "reference not installed in baseline/_ref "
+                                                              "(python oracle/install_reference.py <checkout>)"}),
+              flush=True)
+        return
+    threads = _host_threads()
+    torch.set_num_threads(threads)
+    smp = CpuStep(ref)
+    smp.step(1)  # first touch of the arrays
     t0 = time.perf_counter()
-    smp.step(L // P)  # calibration: one whole 4096-token sequence, warm
+    smp.step(B)  # calibration: one full step
     t_full = time.perf_counter() - t0
-    per_step = min(1.0, 90.0 / max(1, args.steps + args.warmup))
-    pages = int(max(1, min(L // P, round((L // P) * per_step / max(t_full, 1e-6)))))
+    seqs = B
+    if (args.steps + args.warmup) * t_full > 150.0:
+        seqs = max(1, min(B, int(B * 150.0 / ((args.steps + args.warmup) * t_full))))
     for _ in range(args.warmup):
-        smp.step(pages)
+        smp.step(seqs)
     done = 0
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        done += smp.step(pages)
+        done += smp.step(seqs)
     dt = time.perf_counter() - t0
     value = done / dt / 1e12
-    cores = os.cpu_count()
-    desc = (f"{args.steps} steps x (decode of one of 4 config-2 sequences over its first {pages * P} tokens + "
-            f"its 1-token append), numpy oracle, {dt:.1f} s")
+    sample = (f"{args.steps} measured steps, each the eager decode of {seqs} of the 64 sequences x 4096 tokens "
+              f"+ their 1-token appends{'' if seqs == B else ' (a full step would exceed the run budget)'}")
     line = {
-        "impl": "reference", "metric": "decode-attn achieved HBM TB/s (% of B200 peak) + us/step; append tokens/s",
-        "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": STEP_BYTES / (value * 1e12) * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "fp16/int4->fp32", "data": "synthetic",
-        "config": _config(),
-        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": cores, "kind": "port", "sample": desc,
-                         **_cpu_info()},
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16/int4->fp32",
+        "data": "synthetic", "config": _config(world), "step_sequences": seqs, "run_s": dt,
+        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": threads, "kind": "reference",
+                         "code": "torch_eager_int4_paged_decode_attention + torch_eager_append "
+                                 "(baseline/_ref, unmodified)", "sample": sample, "cpu_model": _cpu_model(),
+                         "torch_threads": threads},
         "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def _config():
-    return {"workload": "BASELINE config 2: Llama-3-8B-shaped INT4 paged decode 64 x 4096 + 1-token append",
-            "batch": B, "context": L, "hq": HQ, "hkv": HKV, "head_dim": D, "page_size": P, "group": G,
-            "pool_pages": POOL, "l2": "no flush: each step reads 303 MB of cache > 126 MB L2",
-            "parallelism": "sequence-sharded replicas (one 64x4096 batch per GPU)",
-            "validation": "deferred (value, e2e), synchronous per call (e2e_sync)"}
+METRIC = "decode-attn achieved HBM TB/s (% of B200 peak) + us/step; append tokens/s"
 
+
+def _config(world):
+    return {"workload": "BASELINE config 2: INT4 paged decode 64 x 4096 (Hq 32, Hkv 8, D 128) + 1-token append",
+            "batch": B, "context": L, "page_size": P, "group": G,
+            "parallelism": f"sequence-sharded {B // world if B % world == 0 else '~' + str(B // world)} seqs/GPU"
+                           if world > 1 else "one GPU",
+            "l2": "no flush: 303 MB of cache per step > 126 MB L2"}
+
+
+# ------------------------------------------------------------- config 4 pieces
+
+def _fp32_partial(q, kd, vd, ks, vs, bt_row, ntok, hq):
+    """FP32 (o, lse natural) of one sequence over `ntok` tokens of its local
+    pages, dequantised in torch (an independent restatement for the
+    self-check; not the timed path)."""
+    hkv = kd.shape[2]
+    rep = hq // hkv
+    npg = -(-ntok // P)
+    ids = bt_row[:npg].long()
+    o = torch.empty(hq, D, dtype=torch.float32, device=q.device)
+    lse = torch.empty(hq, dtype=torch.float32, device=q.device)
+
+    def deq(packed, scales):
+        lo = (packed & 0x0F).to(torch.int16)
+        hi = (packed >> 4).to(torch.int16)
+        lo = torch.where(lo >= 8, lo - 16, lo)
+        hi = torch.where(hi >= 8, hi - 16, hi)
+        x = torch.stack((lo, hi), dim=-1).flatten(-2).float()
+        return x * scales.float().repeat_interleave(G, dim=-1)
+
+    for h in range(hkv):
+        k = deq(kd[ids, :, h].reshape(-1, D // 2)[:ntok], ks[ids, :, h].reshape(-1, D // G)[:ntok])
+        v = deq(vd[ids, :, h].reshape(-1, D // 2)[:ntok], vs[ids, :, h].reshape(-1, D // G)[:ntok])
+        logits = (q[h * rep:(h + 1) * rep].float() @ k.T) * (D ** -0.5)
+        lse[h * rep:(h + 1) * rep] = torch.logsumexp(logits, dim=-1)
+        o[h * rep:(h + 1) * rep] = torch.softmax(logits, dim=-1) @ v
+    return o, lse
+
+
+def c4_self_check(c4, dec4, out, dist, rank, world, dev):
+    """Rank 0 compares the split-context output of sequences 0..1 with an
+    FP32 reference assembled from every rank's FP32 partial over its own
+    splits (log-sum-exp merge in fp64).  Every rank takes the same
+    collective steps."""
+    plan = c4["plan"]
+    n = C4_CHECK_SEQS
+    po = torch.zeros(n, C4_HQ, D, dtype=torch.float32, device=dev)
+    pl = torch.full((n, C4_HQ), float("-inf"), dtype=torch.float32, device=dev)
+    for i, b in enumerate(plan.seqs.tolist()):
+        if b < n:
+            po[b], pl[b] = _fp32_partial(c4["q"][b], c4["kd"], c4["vd"], c4["ks"], c4["vs"], dec4.local_bt[i],
+                                         int(plan.lens[i]), C4_HQ)
+    if dist is not None:
+        ao = torch.empty(world, *po.shape, dtype=po.dtype, device=dev)
+        al = torch.empty(world, *pl.shape, dtype=pl.dtype, device=dev)
+        dist.all_gather_into_tensor(ao, po)
+        dist.all_gather_into_tensor(al, pl)
+    else:
+        ao, al = po[None], pl[None]
+    if rank != 0:
+        return None
+    lse = al.double()
+    m = lse.max(dim=0).values
+    w = torch.exp(lse - m)
+    w = w / w.sum(dim=0)
+    ref = (w[..., None] * ao.double()).sum(dim=0).float()
+    got = out[:n].float()
+    err = (got - ref).abs()
+    ok = bool((err <= 2e-3 + 1e-2 * ref.abs()).all() and torch.isfinite(got).all())
+    return {"max_abs_err": float(err.max()), "pass": ok, "seqs": n, "tol": "2e-3 + 1e-2|ref|"}
+
+
+def c4_breakdown(c4, dec4, steps, dev, dist, warmup):
+    """Per-stage device times of the split-context step, each stage replayed
+    from its own graph: the local LSE decode, the NCCL all-gather, the merge.
+    Returns max-over-ranks ms per step of each, and the min over ranks of the
+    decode (the spread is the rank skew the all-gather absorbs)."""
+    from iris_kernel.fused_attention import decode_partial, merge_lse_packed
+
+    plan = dec4.plan
+
+    def dec():
+        decode_partial(c4["q"], c4["kd"], c4["vd"], c4["ks"], c4["vs"], dec4.local_bt, dec4.lens, out=dec4._o,
+                       lse=dec4._lse)
+
+    def gather():
+        dist.all_gather_into_tensor(dec4.recv, dec4.send)
+
+    def merge():
+        merge_lse_packed(dec4.recv if dist is not None else dec4.send, dec4.world, plan.batch, C4_HQ, D,
+                         dec4.output)
+
+    res = {}
+    stages = [("decode", dec), ("merge", merge)] + ([("allgather", gather)] if dist is not None else [])
+    for name, fn in stages:
+        g = graph_of(fn, dev)
+        ms = timed(g.replay, steps, dev, dist, warmup) / steps
+        res[name + "_us"] = reduce_over_ranks(ms, dist, dev) * 1e3
+        if name == "decode":
+            res["decode_us_min_rank"] = reduce_over_ranks(ms, dist, dev, "min") * 1e3
+        del g
+    return res
+
+
+# --------------------------------------------------------------------- main
 
 def main():
     ap = argparse.ArgumentParser()
@@ -530,15 +674,15 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--only", default="all", choices=["all", "c2", "c3", "c4", "c5a", "c5b", "f16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
-    dist, rank, world, local = _dist()
     if args.impl == "reference":
-        run_reference(args, dist, rank, world)
-        if dist is not None:
-            dist.destroy_process_group()
+        # host work only: no process group; under torchrun rank 0 alone runs it
+        run_reference(args, None, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))
         return
+    dist, rank, world, local = _dist()
 
     import iris_kernel
     from iris_kernel.fused_attention import fused_int4_paged_decode_attention
@@ -546,86 +690,188 @@ def main():
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    w = build_workload(dev, seed=1234 + rank)
-
-    # ---- value: graph-replayed steps, inputs resident ----
-    iris_kernel.set_validation_mode("deferred")
-    g_step = graph_of(lambda: (step_decode(w), step_append(w)), dev)
-    g_dec = graph_of(lambda: step_decode(w), dev)
-    g_app = graph_of(lambda: step_append(w), dev)
-    clk = Clocks(local).__enter__()
-    ms = timed(g_step.replay, args.steps, dev, dist, args.warmup)
-    ms_dec = timed(g_dec.replay, args.steps, dev, dist, args.warmup)
-    ms_app = timed(g_app.replay, args.steps, dev, dist, args.warmup)
-    iris_kernel.check_errors(dev)
-    iris_kernel.set_validation_mode("sync")
-    # config 5b prefill append (its own inputs; not part of the step)
-    x = build_prefill(dev, seed=99 + rank)
-    iris_kernel.set_validation_mode("deferred")
-    g_pf = graph_of(lambda: step_prefill(x), dev)
-    pf_steps = max(10, min(args.steps, 200))
-    ms_pf = timed(g_pf.replay, pf_steps, dev, dist, args.warmup)
-    iris_kernel.check_errors(dev)
-    iris_kernel.set_validation_mode("sync")
-    del g_pf, x
-    ms_pf = max_over_ranks(ms_pf, dist, dev)
-    pf_us = ms_pf / pf_steps * 1e3
-    # config 5a decode-style append (2048 x 1 token, Hkv 1; its own inputs)
-    x5 = build_c5a(dev, seed=55 + rank)
-    iris_kernel.set_validation_mode("deferred")
-    g_a5 = graph_of(lambda: step_prefill(x5), dev)
-    ms_a5 = timed(g_a5.replay, pf_steps, dev, dist, args.warmup)
-    iris_kernel.check_errors(dev)
-    iris_kernel.set_validation_mode("sync")
-    del g_a5, x5
-    a5_us = max_over_ranks(ms_a5, dist, dev) / pf_steps * 1e3
-
-    # config 4: split-context decode over the ranks (one NCCL all-gather per step)
-    from iris_kernel import parallel
-
-    c4 = build_c4(dev, rank, world, seed=44 + rank)
-    dec4 = parallel.SplitContextDecoder(c4["plan"], c4["bt"], C4_HQ, D)
-    iris_kernel.set_validation_mode("deferred")
-    g_c4 = graph_of(lambda: dec4(c4["q"], c4["kd"], c4["vd"], c4["ks"], c4["vs"]), dev)
+    run = (lambda name: args.only in ("all", name))
     x_steps = max(10, min(args.steps, 100))
-    ms_c4 = timed(g_c4.replay, x_steps, dev, dist, args.warmup)
-    iris_kernel.check_errors(dev)
-    del g_c4, dec4, c4  # the graph holds an NCCL call: released before the process group
-    # the matched FP16 decode on the config-2 shape (the INT4 cache's baseline)
-    from iris_kernel.fused_attention import fused_fp16_paged_decode_attention
+    peak, peak_kind = _peak_gbs()
+    extra = {}
+    clocks = None
 
-    g16 = torch.Generator(device=dev).manual_seed(16 + rank)
-    kc = (torch.randn(POOL, P, HKV, D, generator=g16, device=dev) * 0.5).half()
-    vc = (torch.randn(POOL, P, HKV, D, generator=g16, device=dev) * 0.5).half()
-    out16 = torch.empty_like(w["q"])
-    g_f16 = graph_of(lambda: fused_fp16_paged_decode_attention(w["q"], kc, vc, w["bt"], w["lens"], out16), dev)
-    ms_f16 = timed(g_f16.replay, x_steps, dev, dist, args.warmup)
-    iris_kernel.check_errors(dev)
-    del g_f16, kc, vc
-    # config 3: sequence-sharded MHA decode, no collective
-    c3 = build_c3(dev, rank, world, seed=33 + rank)
-    g_c3 = graph_of(lambda: fused_int4_paged_decode_attention(c3["q"], c3["kd"], c3["vd"], c3["ks"], c3["vs"],
-                                                              c3["bt"], c3["lens"], c3["out"]), dev)
-    ms_c3 = timed(g_c3.replay, x_steps, dev, dist, args.warmup)
-    iris_kernel.check_errors(dev)
+    # ---- config 2 step: value (graph replay, inputs resident) ----
+    lo, hi = shard(world, rank)
+    nseq = hi - lo
+    if run("c2"):
+        w = build_c2(dev, 1234 + rank, nseq)
+
+        def step_decode():
+            fused_int4_paged_decode_attention(w["q"], w["kd"], w["vd"], w["ks"], w["vs"], w["bt"], w["lens"],
+                                              w["out"])
+
+        def step_append():
+            fused_rope_int4_paged_append(w["knew"], w["vnew"], w["newpos"], w["newslot"], w["cos"], w["sin"],
+                                         w["kd"], w["vd"], w["ks"], w["vs"], rotary_dim=D, page_size=P)
+
+        iris_kernel.set_validation_mode("deferred")
+        g_step = graph_of(lambda: (step_decode(), step_append()), dev)
+        g_dec = graph_of(step_decode, dev)
+        g_app = graph_of(step_append, dev)
+        clk = Clocks(local).__enter__()
+        ms = timed(g_step.replay, args.steps, dev, dist, args.warmup)
+        d_steps = max(args.steps, 200)
+        ms_dec = timed(g_dec.replay, d_steps, dev, dist, args.warmup) / d_steps
+        ms_app = timed(g_app.replay, d_steps, dev, dist, args.warmup) / d_steps
+        iris_kernel.check_errors(dev)
+        del g_step, g_dec, g_app
+        ms = reduce_over_ranks(ms, dist, dev)
+        dec_us = reduce_over_ranks(ms_dec, dist, dev) * 1e3
+        app_us = reduce_over_ranks(ms_app, dist, dev) * 1e3
+        step_ms = ms / args.steps
+        e2e = run_e2e(w, args, dev, dist, world)
+        clk.__exit__(None, None, None)
+        clocks = clk.summary()
+        del w
+    # ---- config 5b prefill append and config 5a decode-style append ----
+    if run("c5b"):
+        x = build_prefill(dev, seed=99 + rank)
+        iris_kernel.set_validation_mode("deferred")
+        g_pf = graph_of(lambda: fused_rope_int4_paged_append(x["k"], x["v"], x["pos"], x["slots"], x["cos"],
+                                                             x["sin"], x["kd"], x["vd"], x["ks"], x["vs"],
+                                                             rotary_dim=D, page_size=P), dev)
+        pf_us = reduce_over_ranks(timed(g_pf.replay, x_steps, dev, dist, args.warmup), dist, dev) / x_steps * 1e3
+        iris_kernel.check_errors(dev)
+        del g_pf, x
+        extra["c5b"] = {"us": pf_us, "tbs": world * PF_BYTES / (pf_us * 1e-6) / 1e12,
+                        "frac": PF_BYTES / (pf_us * 1e-6) / 1e9 / peak,
+                        "tokens_per_s": world * PF_S * PF_L / (pf_us * 1e-6)}
+    if run("c5a"):
+        x5 = build_c5a(dev, seed=55 + rank)
+        iris_kernel.set_validation_mode("deferred")
+        g_a5 = graph_of(lambda: fused_rope_int4_paged_append(x5["k"], x5["v"], x5["pos"], x5["slots"], x5["cos"],
+                                                             x5["sin"], x5["kd"], x5["vd"], x5["ks"], x5["vs"],
+                                                             rotary_dim=D, page_size=P), dev)
+        a5_us = reduce_over_ranks(timed(g_a5.replay, x_steps, dev, dist, args.warmup), dist, dev) / x_steps * 1e3
+        iris_kernel.check_errors(dev)
+        del g_a5, x5
+        extra["c5a"] = {"us": a5_us, "tokens_per_s": world * A5_T / (a5_us * 1e-6)}
+    # ---- config 4: split-context decode over the ranks (one NCCL all-gather per step) ----
+    if run("c4"):
+        from iris_kernel import parallel
+
+        c4 = build_c4(dev, rank, world, seed=44 + rank)
+        dec4 = parallel.SplitContextDecoder(c4["plan"], c4["bt"], C4_HQ, D)
+        iris_kernel.set_validation_mode("deferred")
+        g_c4 = graph_of(lambda: dec4(c4["q"], c4["kd"], c4["vd"], c4["ks"], c4["vs"]), dev)
+        ms_c4 = timed(g_c4.replay, x_steps, dev, dist, args.warmup)
+        iris_kernel.check_errors(dev)
+        del g_c4  # the graph holds an NCCL call: released before the process group
+        c4_us = reduce_over_ranks(ms_c4, dist, dev) / x_steps * 1e3
+        parts = c4_breakdown(c4, dec4, x_steps, dev, dist, args.warmup)
+        iris_kernel.set_validation_mode("sync")
+        out4 = dec4(c4["q"], c4["kd"], c4["vd"], c4["ks"], c4["vs"])
+        torch.cuda.synchronize(dev)
+        check = c4_self_check(c4, dec4, out4, dist, rank, world, dev)
+        extra["c4"] = {"us": c4_us, "tbs": C4_BYTES / (c4_us * 1e-6) / 1e12,
+                       "frac": C4_BYTES / (c4_us * 1e-6) / 1e9 / (world * peak),
+                       **{k: round(v, 2) for k, v in parts.items()}, "check": check}
+        del dec4, c4
+    # ---- the matched FP16 decode on the config-2 shape ----
+    if run("f16") and world == 1:
+        from iris_kernel.fused_attention import fused_fp16_paged_decode_attention
+
+        g16 = torch.Generator(device=dev).manual_seed(16 + rank)
+        pool = B * (L // P + 1)
+        kc = (torch.randn(pool, P, HKV, D, generator=g16, device=dev) * 0.5).half()
+        vc = (torch.randn(pool, P, HKV, D, generator=g16, device=dev) * 0.5).half()
+        q16 = torch.randn(B, HQ, D, generator=g16, device=dev).half()
+        bt16 = torch.randperm(pool, generator=g16, device=dev).int().view(B, L // P + 1).contiguous()
+        lens16 = torch.full((B,), L, dtype=torch.int32, device=dev)
+        out16 = torch.empty_like(q16)
+        iris_kernel.set_validation_mode("deferred")
+        g_f16 = graph_of(lambda: fused_fp16_paged_decode_attention(q16, kc, vc, bt16, lens16, out16), dev)
+        f16_us = timed(g_f16.replay, x_steps, dev, dist, args.warmup) / x_steps * 1e3
+        iris_kernel.check_errors(dev)
+        del g_f16, kc, vc
+        extra["f16"] = {"us": f16_us, "tbs": FP16_BYTES / (f16_us * 1e-6) / 1e12,
+                        "frac": FP16_BYTES / (f16_us * 1e-6) / 1e9 / peak}
+    # ---- config 3: sequence-sharded MHA decode, no collective ----
+    if run("c3"):
+        c3 = build_c3(dev, rank, world, seed=33 + rank)
+        iris_kernel.set_validation_mode("deferred")
+        g_c3 = graph_of(lambda: fused_int4_paged_decode_attention(c3["q"], c3["kd"], c3["vd"], c3["ks"], c3["vs"],
+                                                                  c3["bt"], c3["lens"], c3["out"]), dev)
+        c3_us = reduce_over_ranks(timed(g_c3.replay, x_steps, dev, dist, args.warmup), dist, dev) / x_steps * 1e3
+        iris_kernel.check_errors(dev)
+        extra["c3"] = {"us": c3_us, "tbs": c3["total_bytes"] / (c3_us * 1e-6) / 1e12,
+                       "frac": c3["total_bytes"] / (c3_us * 1e-6) / 1e9 / (world * peak)}
+        del g_c3, c3
     iris_kernel.set_validation_mode("sync")
-    c3_total = c3["total_bytes"]
-    del g_c3, c3
-    f16_us = max_over_ranks(ms_f16, dist, dev) / x_steps * 1e3
-    c4_us = max_over_ranks(ms_c4, dist, dev) / x_steps * 1e3
-    c3_us = max_over_ranks(ms_c3, dist, dev) / x_steps * 1e3
-    ms = max_over_ranks(ms, dist, dev)
-    ms_dec = max_over_ranks(ms_dec, dist, dev)
-    ms_app = max_over_ranks(ms_app, dist, dev)
-    step_ms = ms / args.steps
-    dec_us = ms_dec / args.steps * 1e3
-    app_us = ms_app / args.steps * 1e3
-    value = world * STEP_BYTES / (step_ms * 1e-3) / 1e12
 
-    # ---- e2e: public API with host buffers ----
-    # The step's inputs (new query, K, V, positions, slots) sit in one pinned
-    # host buffer and go to the device in one copy; the fp16 output comes back
-    # in one copy.
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and run("c2"):
+        cpu = cpu_baseline_sample(seconds_budget=15.0)
+
+    if rank == 0:
+        if not run("c2"):
+            print(json.dumps({"only": args.only, "n_gpus": world, **extra, "clocks": clocks}), flush=True)
+        else:
+            dec_local = decode_bytes(nseq)
+            achieved = dec_local / (dec_us * 1e-6) / 1e9
+            traffic = None
+            tpath = os.path.join(ROOT, "profiles", "decode_c2_traffic.json")
+            if os.path.exists(tpath) and world == 1:
+                try:
+                    with open(tpath) as f:
+                        traffic = json.load(f).get("dram_bytes_per_launch")
+                except Exception:
+                    traffic = None
+            value = STEP_BYTES / (step_ms * 1e-3) / 1e12
+            compact = {}
+            for k in ("c3", "c4"):
+                if k in extra:
+                    compact[k + "_us"] = round(extra[k]["us"], 2)
+                    compact[k + "_frac"] = round(extra[k]["frac"], 3)
+            if "c4" in extra and extra["c4"]["check"] is not None:
+                compact["c4_max_abs_err"] = extra["c4"]["check"]["max_abs_err"]
+                compact["c4_parity"] = extra["c4"]["check"]["pass"]
+            line = {
+                "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, **compact,
+                "dtype": "fp16/int4->fp32", "data": "synthetic (seeded N(0,1), random page permutation)",
+                "config": _config(world),
+                "decode_us": dec_us, "decode_tbs": dec_local / (dec_us * 1e-6) / 1e12,
+                "decode_pct_of_8tbs": 100 * dec_local / (dec_us * 1e-6) / 1e12 / SPEC_TBS,
+                "append_us": app_us, "append_tokens_per_s": B / (app_us * 1e-6),
+                "e2e": e2e,
+                "gpu_launches": 3 * args.steps,  # decode, combine, append per step (graph replay)
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                             "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic,
+                             "kernel": "decode + combine (graph), per GPU"},
+                "cpu_baseline": cpu, "clocks": clocks, **{k: _round(v) for k, v in extra.items()},
+            }
+            print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _round(d):
+    if isinstance(d, dict):
+        return {k: _round(v) for k, v in d.items()}
+    if isinstance(d, float):
+        return float(f"{d:.4g}")
+    return d
+
+
+def run_e2e(w, args, dev, dist, world):
+    """The step through the public Python API with host buffers (deferred
+    validation, the step's error word read on the host once per step).  The
+    query copy leads; the decode starts as soon as it has landed, the new
+    K/V copy runs meanwhile on a second stream, the append waits for it, and
+    the output copy overlaps the append.  Returns the line's e2e object."""
+    import iris_kernel
+    from iris_kernel.fused_attention import fused_int4_paged_decode_attention
+    from iris_kernel.fused_kv import fused_rope_int4_paged_append
+
     parts = [("q", w["q"]), ("k", w["knew"]), ("v", w["vnew"]), ("p", w["newpos"]), ("s", w["newslot"])]
     offs, total = {}, 0
     for name, t in parts:
@@ -644,115 +890,48 @@ def main():
     h2d = sum(t.numel() * t.element_size() for _, t in parts)
     d2h = hout.numel() * hout.element_size()
     q, k, v, pp, ss = (view(dev_in, name, t) for name, t in parts)
+    q_bytes = offs["k"]
     out_dev = torch.empty_like(w["out"])
+    main = torch.cuda.current_stream(dev)
+    side = torch.cuda.Stream(dev)
+    kv_ready, out_ready = torch.cuda.Event(), torch.cuda.Event()
+    calls = {"dec": lambda: fused_int4_paged_decode_attention(q, w["kd"], w["vd"], w["ks"], w["vs"], w["bt"],
+                                                              w["lens"], out_dev),
+             "app": lambda: fused_rope_int4_paged_append(k, v, pp, ss, w["cos"], w["sin"], w["kd"], w["vd"], w["ks"],
+                                                         w["vs"], rotary_dim=D, page_size=P)}
 
-    def calls():
-        fused_int4_paged_decode_attention(q, w["kd"], w["vd"], w["ks"], w["vs"], w["bt"], w["lens"], out_dev)
-        fused_rope_int4_paged_append(k, v, pp, ss, w["cos"], w["sin"], w["kd"], w["vd"], w["ks"], w["vs"],
-                                     rotary_dim=D, page_size=P)
+    def e2e_step():
+        dev_in[:q_bytes].copy_(host_in[:q_bytes], non_blocking=True)
+        with torch.cuda.stream(side):
+            side.wait_stream(main)
+            dev_in[q_bytes:].copy_(host_in[q_bytes:], non_blocking=True)
+            kv_ready.record(side)
+        calls["dec"]()
+        out_ready.record(main)
+        main.wait_event(kv_ready)
+        calls["app"]()
+        with torch.cuda.stream(side):
+            side.wait_event(out_ready)
+            hout.copy_(out_dev, non_blocking=True)
+        main.wait_stream(side)
+        iris_kernel.check_errors(dev)  # one host read of the error word per step (syncs)
 
-    def e2e_step(replay=None):
-        dev_in.copy_(host_in, non_blocking=True)
-        if replay is None:
-            calls()
-        else:
-            replay()
-        hout.copy_(out_dev, non_blocking=True)
-        if iris_kernel.validation_mode() == "deferred":
-            iris_kernel.check_errors(dev)  # one host read per step raises any error of the step
-
-    # e2e: eager calls, deferred validation, errors raised once per step (the
-    # host prepares the next call while the GPU runs).  e2e_sync: every call
-    # reads the error word before it returns, as the reference's calls raise.
-    # e2e_graph: the two calls captured once in a CUDA graph and replayed.
     iris_kernel.set_validation_mode("deferred")
-    ms_e2e = timed(e2e_step, args.steps, dev, dist, args.warmup)
-    g_e2e = graph_of(calls, dev)
-    ms_e2e_graph = timed(lambda: e2e_step(g_e2e.replay), args.steps, dev, dist, args.warmup)
+    ms = timed(e2e_step, args.steps, dev, dist, args.warmup)
+    # the same step with each call replayed from a CUDA graph captured once
+    graphs = {n: graph_of(fn, dev) for n, fn in calls.items()}
+    step_calls = dict(calls)
+    calls["dec"], calls["app"] = graphs["dec"].replay, graphs["app"].replay
+    ms_graph = timed(e2e_step, args.steps, dev, dist, args.warmup)
+    calls.update(step_calls)
+    del graphs
     iris_kernel.set_validation_mode("sync")
-    ms_e2e_sync = timed(e2e_step, args.steps, dev, dist, args.warmup)
-    del g_e2e
-    clk.__exit__(None, None, None)
-    ms_e2e = max_over_ranks(ms_e2e, dist, dev)
-    ms_e2e_sync = max_over_ranks(ms_e2e_sync, dist, dev)
-    ms_e2e_graph = max_over_ranks(ms_e2e_graph, dist, dev)
-    e2e_value = world * STEP_BYTES / (ms_e2e / args.steps * 1e-3) / 1e12
-    e2e_sync_value = world * STEP_BYTES / (ms_e2e_sync / args.steps * 1e-3) / 1e12
-    e2e_graph_value = world * STEP_BYTES / (ms_e2e_graph / args.steps * 1e-3) / 1e12
-
-    clocks = clk.summary()
-    peak, peak_kind = _peak_gbs()
-    achieved = DECODE_BYTES / (dec_us * 1e-6) / 1e9
-    traffic = None
-    tpath = os.path.join(ROOT, "profiles", "decode_c2_traffic.json")
-    if os.path.exists(tpath):
-        try:
-            traffic = json.load(open(tpath)).get("dram_bytes_per_launch")
-        except Exception:
-            traffic = None
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, desc, _ = cpu_baseline_sample(seconds_budget=15.0)
-        cpu = {"value": v, "unit": "TB/s", "cores": os.cpu_count(), "kind": "port", "sample": desc, **_cpu_info()}
-
-    if rank == 0:
-        line = {
-            "metric": "decode-attn achieved HBM TB/s (% of B200 peak) + us/step; append tokens/s",
-            "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "fp16/int4->fp32", "data": "synthetic (seeded N(0,1), random page permutation)",
-            "config": _config(),
-            "us_per_step": step_ms * 1e3,
-            "decode_us": dec_us, "decode_tbs": DECODE_BYTES / (dec_us * 1e-6) / 1e12,
-            "decode_pct_of_8tbs": 100 * DECODE_BYTES / (dec_us * 1e-6) / 1e12 / SPEC_TBS,
-            "decode_pct_of_measured": 100 * achieved / peak,
-            "append_us": app_us, "append_tokens_per_s": world * B / (app_us * 1e-6),
-            "prefill_append": {"config": "BASELINE config 5b: 8 x 8192 tokens, Hkv 8, D 128",
-                               "us": pf_us, "tbs": world * PF_BYTES / (pf_us * 1e-6) / 1e12,
-                               "pct_of_measured": 100 * PF_BYTES / (pf_us * 1e-6) / 1e9 / _peak_gbs()[0],
-                               "tokens_per_s": world * PF_S * PF_L / (pf_us * 1e-6), "bytes": PF_BYTES},
-            "config5a_append": {"config": "BASELINE config 5a: 2048 sequences x 1 token, Hkv 1, D 128, "
-                                          "positions ~U[0, 32768)",
-                                "us": a5_us, "tbs": world * A5_BYTES / (a5_us * 1e-6) / 1e12,
-                                "tokens_per_s": world * A5_T / (a5_us * 1e-6), "bytes": A5_BYTES},
-            "config4_split_context": {
-                "config": "BASELINE config 4: 16 x 131072 tokens, Hq 64, Hkv 8, D 128, 8192-token splits dealt "
-                          "over the ranks; each rank's cache holds only its splits",
-                "us": c4_us, "tbs": C4_BYTES / (c4_us * 1e-6) / 1e12, "bytes": C4_BYTES,
-                "collective": "one NCCL all_gather_into_tensor of packed (O, lse) fp32 per step" if world > 1
-                              else "none (one GPU)"},
-            "fp16_decode_c2": {
-                "config": "matched FP16 paged decode on the config-2 shape (64 x 4096, Hq 32, Hkv 8, D 128)",
-                "us": f16_us, "tbs": FP16_BYTES / (f16_us * 1e-6) / 1e12, "bytes": FP16_BYTES,
-                "int4_speedup": f16_us / dec_us},
-            "config3_sharded": {
-                "config": "BASELINE config 3: 128 sequences, L ~ U[1,16384] (seed 1), Hq = Hkv = 16, D 64; "
-                          "whole sequences sharded over the ranks by token count, no collective",
-                "us": c3_us, "tbs": c3_total / (c3_us * 1e-6) / 1e12, "bytes": c3_total},
-            "step_bytes": STEP_BYTES, "decode_bytes": DECODE_BYTES, "append_bytes": APPEND_BYTES,
-            "e2e": {"value": e2e_value, "unit": "TB/s", "ms_per_step": ms_e2e / args.steps,
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "validation": "deferred, errors raised once per step (iris_kernel.check_errors)"},
-            "e2e_sync": {"value": e2e_sync_value, "unit": "TB/s", "ms_per_step": ms_e2e_sync / args.steps,
-                         "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                         "validation": "synchronous: every call reads the error word before returning"},
-            "e2e_graph": {"value": e2e_graph_value, "unit": "TB/s", "ms_per_step": ms_e2e_graph / args.steps,
-                          "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                          "validation": "deferred, errors raised once per step; the two calls replayed from a "
-                                        "CUDA graph captured once"},
-            "gpu_launches": 3 * args.steps,  # decode, combine, append (a 64-token batch validates itself)
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_kind": peak_kind, "traffic": traffic,
-                         "kernel": "decode (decode + combine launches) timed alone from a CUDA graph"},
-            "cpu_baseline": cpu,
-            "clocks": clocks,
-        }
-        print(json.dumps(line), flush=True)
-    del g_step, g_dec, g_app
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+    ms = reduce_over_ranks(ms, dist, dev)
+    ms_graph = reduce_over_ranks(ms_graph, dist, dev)
+    return {"value": STEP_BYTES / (ms / args.steps * 1e-3) / 1e12, "unit": "TB/s", "ms_per_step": ms / args.steps,
+            "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+            "path": "public Python API, deferred validation, error word read per step",
+            "graph_ms_per_step": ms_graph / args.steps}
 
 
 if __name__ == "__main__":

@@ -67,6 +67,22 @@ IRIS_API int iris_b200_version(void);
  */
 IRIS_API int iris_b200_selftest_bounded_wait(int32_t* error_word, int64_t limit_ns, void* stream);
 
+/*
+ * Self-test of the write path's division-free quantiser over its whole finite
+ * domain.  For every group absmax with non-negative finite fp16 bit pattern
+ * in [amax_lo, amax_hi) (0 <= amax_lo < amax_hi <= 0x7C00) and every fp16 x
+ * with |x| <= amax, the append's quantiser (scale = fp16(max(amax/7, 2^-14))
+ * from a Markstein-corrected reciprocal, q from a corrected reciprocal and a
+ * round-half-even magic add) is compared with the reference's arithmetic in
+ * IEEE operations (torch_eager_kv.py:77-86: amax / 7.0, x / scale, round,
+ * clamp).  Adds to counts[0] the 8-value packed words that differ, to
+ * counts[1] the amax values whose fp16 scale differs and to counts[2] the
+ * words compared (device pointer to three uint64, zeroed by the caller).
+ * No counterpart in the reference.
+ */
+IRIS_API int iris_b200_selftest_quantizer_sweep(int32_t amax_lo, int32_t amax_hi, unsigned long long* counts,
+                                                void* stream);
+
 /* Human-readable text for a status code. */
 IRIS_API const char* iris_b200_status_string(int status);
 
@@ -238,11 +254,16 @@ IRIS_API int iris_b200_fp16_paged_decode(const void* query, const void* k_cache,
  * device memory, code running in allocator or stream callbacks, serving loops
  * that forbid allocation after start-up).
  *   - Nothing is allocated; returns IRIS_EWORKSPACE, before touching the
- *     array, when the problem needs more scratch than the array holds
- *     (iris_b200_decode_workspace_bytes > IRIS_DECODE_NOALLOC_SCRATCH_BYTES).
+ *     array, when the problem needs more scratch than the array holds.  The
+ *     need is sized by the problem: at most ceil(batch * max_pages_per_seq / 4)
+ *     split-KV ranges (and never more than the GPU-wide maximum that
+ *     iris_b200_decode_workspace_bytes assumes), each holding two records of
+ *     num_q_heads * (head_dim + 1) floats.
  *   - The first call on a device looks up the array's device address
  *     (cudaGetSymbolAddress) with that device current; make that first call
- *     before any stream capture.
+ *     before any stream capture.  The address (like the library's cached
+ *     launch shapes and tensor maps) is kept for the life of the process and
+ *     does not survive cudaDeviceReset or a re-created primary context.
  *   - All calls share the one array: calls whose work overlaps on the GPU
  *     (other streams, other host threads) race.  Each call rewrites the
  *     parts it reads, so no state carries over between calls.

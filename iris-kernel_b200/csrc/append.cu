@@ -775,3 +775,71 @@ extern "C" int iris_b200_rope_fp16_paged_append(const void* key, const void* val
   }
   return IRIS_OK;
 }
+
+namespace {
+
+// Exhaustive check of the division-free quantiser (group_scale +
+// quant_pack_vec, the finite-scale path of every INT4 append) against the
+// reference's arithmetic written with IEEE operations: scale =
+// fp16(max(amax / 7, 2^-14)) with __fdiv_rn, q = clamp(rint(x / scale), -7, 7)
+// with __fdiv_rn and __float2int_rn.  blockIdx.y selects the group absmax
+// (non-negative finite fp16 bit pattern amax_lo + blockIdx.y); each thread
+// takes 8 consecutive magnitudes x <= amax (both signs: every fp16 x with
+// |x| <= amax is reachable in a group with that absmax) and compares the two
+// packed words.  Magnitudes above amax are replaced by 0 (the same q = 0 on
+// both paths).  counts[0] += mismatching words, counts[1] += amax values
+// whose scale differs, counts[2] += words compared.
+__global__ void __launch_bounds__(256) quantizer_sweep_kernel(uint32_t amax_lo, unsigned long long* counts) {
+  const uint32_t amax_bits = amax_lo + blockIdx.y;
+  const uint32_t m0 = 8u * (blockIdx.x * blockDim.x + threadIdx.x);
+  const __half amax = __ushort_as_half(static_cast<unsigned short>(amax_bits));
+  const __half s16 = iris::group_scale(amax);
+  if (m0 == 0) {
+    const float a = __half2float(amax);
+    float s = __fdiv_rn(a, 7.0f);
+    s = s < 6.103515625e-05f ? 6.103515625e-05f : s;
+    if (__half_as_ushort(__float2half_rn(s)) != __half_as_ushort(s16)) atomicAdd(counts + 1, 1ull);
+  }
+  if (m0 > amax_bits) return;
+  const float sc = __half2float(s16);
+  const float r = iris::rcp_approx(sc);
+  unsigned long long bad = 0;
+#pragma unroll
+  for (int sign = 0; sign < 2; ++sign) {
+    uint4 raw;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t lo = m0 + 2 * i, hi = m0 + 2 * i + 1;
+      lo = lo <= amax_bits ? lo | (sign << 15) : 0u;
+      hi = hi <= amax_bits ? hi | (sign << 15) : 0u;
+      w[i] = lo | (hi << 16);
+    }
+    const __half2* v = reinterpret_cast<const __half2*>(&raw);
+    const __half2 vv[4] = {v[0], v[1], v[2], v[3]};
+    bad += iris::quant_pack_vec(raw, sc, r) != iris::quant_pack8_ieee(vv, sc) ? 1ull : 0ull;
+  }
+  if (bad) atomicAdd(counts, bad);
+  const unsigned active = __activemask();
+  if ((threadIdx.x & 31) == __ffs(active) - 1) atomicAdd(counts + 2, 2ull * __popc(active));
+}
+
+}  // namespace
+
+extern "C" int iris_b200_selftest_quantizer_sweep(int32_t amax_lo, int32_t amax_hi, unsigned long long* counts,
+                                                  void* stream) {
+  if (counts == nullptr || amax_lo < 0 || amax_hi > 0x7C00 || amax_lo >= amax_hi) return IRIS_EINVAL;
+  clear_stale_cuda_error();
+  const uint32_t n = static_cast<uint32_t>(amax_hi - amax_lo);
+  // magnitudes 0 .. amax_hi - 1, 8 per thread
+  const uint32_t threads = 256, per_block = 8 * threads;
+  const dim3 grid((static_cast<uint32_t>(amax_hi) + per_block - 1) / per_block, n);
+  quantizer_sweep_kernel<<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<uint32_t>(amax_lo),
+                                                                                 counts);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    record_cuda_error(e, "quantizer_sweep_kernel launch");
+    return IRIS_ECUDA;
+  }
+  return IRIS_OK;
+}

@@ -1940,6 +1940,26 @@ cudaError_t launch_decode(const Plan& pl, const CUtensorMap& km, const CUtensorM
 
 }  // namespace
 
+// Page ranges a problem can use at most: the plan never cuts fewer than
+// kMinPagesPerRange pages per range, and a batch holds at most
+// batch * max_pages_per_seq pages.
+int32_t problem_ranges(int32_t batch, int32_t max_pages_per_seq) {
+  const int64_t pages = static_cast<int64_t>(batch) * (max_pages_per_seq > 0 ? max_pages_per_seq : 1);
+  const int64_t r = (pages + kMinPagesPerRange - 1) / kMinPagesPerRange;
+  return static_cast<int32_t>(r < 1 ? 1 : (r > 0x7fffffff ? 0x7fffffff : r));
+}
+
+// Workspace bytes of a decode whose page ranges are capped by the problem
+// (the allocation-free entry point carves its fixed array this way).
+size_t problem_workspace_bytes(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                               int32_t max_pages_per_seq, int32_t device) {
+  if (batch <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || (head_dim != 64 && head_dim != 128)) return 0;
+  if (num_q_heads % num_kv_heads != 0) return 0;
+  int32_t r = max_ranges_for(num_q_heads / num_kv_heads, num_kv_heads, device_sms(device));
+  const int32_t cap = problem_ranges(batch, max_pages_per_seq);
+  return carve(nullptr, batch, num_q_heads, head_dim, cap < r ? cap : r).bytes;
+}
+
 extern "C" size_t iris_b200_decode_workspace_bytes(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
                                                    int32_t head_dim, int32_t device) {
   if (batch <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || (head_dim != 64 && head_dim != 128)) return 0;
@@ -1949,14 +1969,15 @@ extern "C" size_t iris_b200_decode_workspace_bytes(int32_t batch, int32_t num_q_
       .bytes;
 }
 
+// ranges_limit > 0 caps the page ranges (and so the workspace carve) below the
+// SM-derived maximum; 0 keeps the maximum.
 static int decode_entry(bool fp16, const void* query, const void* k_data, const void* v_data,
-                                           const void* k_scale, const void* v_scale, const int32_t* block_table,
-                                           int64_t block_table_stride, const int32_t* seq_lens, void* output,
-                                           float* out_lse, int32_t out_mode, int32_t batch, int32_t num_q_heads,
-                                           int32_t num_kv_heads, int32_t head_dim, int64_t num_pages,
-                                           int32_t page_size, int32_t max_pages_per_seq, float softmax_scale,
-                                           void* workspace, size_t workspace_bytes, int32_t* error_word,
-                                           void* stream) {
+                        const void* k_scale, const void* v_scale, const int32_t* block_table,
+                        int64_t block_table_stride, const int32_t* seq_lens, void* output, float* out_lse,
+                        int32_t out_mode, int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                        int32_t head_dim, int64_t num_pages, int32_t page_size, int32_t max_pages_per_seq,
+                        float softmax_scale, void* workspace, size_t workspace_bytes, int32_t* error_word,
+                        void* stream, int32_t ranges_limit = 0) {
   if (batch < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || num_pages <= 0 || max_pages_per_seq < 0)
     return IRIS_EINVAL;
   if (page_size != kPage || (head_dim != 64 && head_dim != 128)) return IRIS_EUNSUPPORTED;
@@ -1984,7 +2005,8 @@ static int decode_entry(bool fp16, const void* query, const void* k_data, const 
     record_cuda_error(e0, "cudaGetDevice");
     return IRIS_ECUDA;
   }
-  const int32_t max_ranges = max_ranges_for(qpk, num_kv_heads, device_sms(device), fp16);
+  int32_t max_ranges = max_ranges_for(qpk, num_kv_heads, device_sms(device), fp16);
+  if (ranges_limit > 0 && ranges_limit < max_ranges) max_ranges = ranges_limit;
   const Workspace ws = carve(workspace, batch, num_q_heads, head_dim, max_ranges);
   if (workspace_bytes < ws.bytes) return IRIS_EWORKSPACE;
 
@@ -2042,6 +2064,20 @@ extern "C" int iris_b200_int4_paged_decode(const void* query, const void* k_data
   return decode_entry(false, query, k_data, v_data, k_scale, v_scale, block_table, block_table_stride, seq_lens,
                       output, out_lse, out_mode, batch, num_q_heads, num_kv_heads, head_dim, num_pages, page_size,
                       max_pages_per_seq, softmax_scale, workspace, workspace_bytes, error_word, stream);
+}
+
+// The INT4 decode with its page ranges capped by the problem size (used by
+// the allocation-free entry point, whose scratch is carved the same way).
+int iris_decode_problem_sized(const void* query, const void* k_data, const void* v_data, const void* k_scale,
+                              const void* v_scale, const int32_t* block_table, int64_t block_table_stride,
+                              const int32_t* seq_lens, void* output, float* out_lse, int32_t out_mode, int32_t batch,
+                              int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int64_t num_pages,
+                              int32_t page_size, int32_t max_pages_per_seq, float softmax_scale, void* workspace,
+                              size_t workspace_bytes, int32_t* error_word, void* stream) {
+  return decode_entry(false, query, k_data, v_data, k_scale, v_scale, block_table, block_table_stride, seq_lens,
+                      output, out_lse, out_mode, batch, num_q_heads, num_kv_heads, head_dim, num_pages, page_size,
+                      max_pages_per_seq, softmax_scale, workspace, workspace_bytes, error_word, stream,
+                      problem_ranges(batch, max_pages_per_seq));
 }
 
 extern "C" size_t iris_b200_fp16_decode_workspace_bytes(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,

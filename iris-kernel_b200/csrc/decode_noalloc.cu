@@ -23,6 +23,19 @@
 
 #include "common.cuh"
 
+// From decode.cu (library-internal, not exported): the workspace a decode
+// needs when its page ranges are capped by the problem (batch *
+// max_pages_per_seq pages at most, at least 4 pages per range) rather than by
+// the GPU's SM count, and the INT4 decode entry that applies that cap.
+size_t problem_workspace_bytes(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                               int32_t max_pages_per_seq, int32_t device);
+int iris_decode_problem_sized(const void* query, const void* k_data, const void* v_data, const void* k_scale,
+                              const void* v_scale, const int32_t* block_table, int64_t block_table_stride,
+                              const int32_t* seq_lens, void* output, float* out_lse, int32_t out_mode, int32_t batch,
+                              int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int64_t num_pages,
+                              int32_t page_size, int32_t max_pages_per_seq, float softmax_scale, void* workspace,
+                              size_t workspace_bytes, int32_t* error_word, void* stream);
+
 namespace {
 
 static __device__ __align__(256) unsigned char g_decode_scratch[IRIS_DECODE_NOALLOC_SCRATCH_BYTES];
@@ -65,13 +78,16 @@ extern "C" int iris_b200_int4_paged_decode_noalloc(const void* query, const void
   }
   if (device < 0 || device >= kMaxDevices) return IRIS_EUNSUPPORTED;
   // The problem must fit the static array; the size is checked before the
-  // array is touched.
-  const size_t need = iris_b200_decode_workspace_bytes(batch, num_q_heads, num_kv_heads, head_dim, device);
+  // array is touched.  The split-KV ranges are capped by the problem's page
+  // count (not only by the SM count), so small problems need little scratch.
+  const size_t need =
+      problem_workspace_bytes(batch, num_q_heads, num_kv_heads, head_dim, max_pages_per_seq, device);
+  if (batch > 0 && need == 0) return IRIS_EINVAL;
   if (need > static_cast<size_t>(IRIS_DECODE_NOALLOC_SCRATCH_BYTES)) return IRIS_EWORKSPACE;
   void* scratch = scratch_on_device(device);
   if (scratch == nullptr) return IRIS_ECUDA;
-  return iris_b200_int4_paged_decode(query, k_data, v_data, k_scale, v_scale, block_table, block_table_stride,
-                                     seq_lens, output, out_lse, out_mode, batch, num_q_heads, num_kv_heads,
-                                     head_dim, num_pages, page_size, max_pages_per_seq, softmax_scale, scratch,
-                                     static_cast<size_t>(IRIS_DECODE_NOALLOC_SCRATCH_BYTES), error_word, stream);
+  return iris_decode_problem_sized(query, k_data, v_data, k_scale, v_scale, block_table, block_table_stride,
+                                   seq_lens, output, out_lse, out_mode, batch, num_q_heads, num_kv_heads, head_dim,
+                                   num_pages, page_size, max_pages_per_seq, softmax_scale, scratch,
+                                   static_cast<size_t>(IRIS_DECODE_NOALLOC_SCRATCH_BYTES), error_word, stream);
 }

@@ -55,6 +55,7 @@ SIGNATURES = {
     "iris_b200_merge_lse_partials": (ctypes.c_int, [_c_p, _c_p, _c_i32, _c_i64, _c_i32, _c_p, _c_p]),
     "iris_b200_merge_lse_packed": (ctypes.c_int, [_c_p, _c_i32, _c_i64, _c_i32, _c_p, _c_p]),
     "iris_b200_selftest_bounded_wait": (ctypes.c_int, [_c_p, _c_i64, _c_p]),
+    "iris_b200_selftest_quantizer_sweep": (ctypes.c_int, [_c_i32, _c_i32, _c_p, _c_p]),
     "iris_b200_int4_quantize_pack": (ctypes.c_int, [_c_p, _c_p, _c_p, _c_i64, _c_i32, _c_p]),
     "iris_b200_rope_fp16_paged_append": (
         ctypes.c_int,

@@ -158,3 +158,74 @@ def workspace_bytes(fn, *shape) -> int:
         if len(_ws_sizes) < 4096:
             _ws_sizes[key] = n
     return n
+
+
+# ---------------------------------------------------------------- fast path
+# A wrapper call whose tensors (device address, shape, strides, dtype) and
+# keyword arguments equal those of an earlier call that passed every host
+# check needs no new checks: the host checks depend on nothing else (the
+# data-dependent ones run on the device).  The prepared C-ABI arguments of
+# such calls are kept per (signature, stream), so a repeated call (a decode
+# loop over the same cache) is one dictionary lookup and one C call.  Device
+# addresses identify the device too (unified virtual addressing).
+
+_FAST_MAX = 512
+
+
+class FastEntry:
+    __slots__ = ("calls", "device", "stream", "keep")
+
+    def __init__(self, calls, device, stream, keep):
+        self.calls = calls    # [(C function, argument list, output slot or -1, what)]
+        self.device = device  # CUDA device index
+        self.stream = stream  # raw stream the arguments were prepared for
+        self.keep = keep      # tensors the arguments point into (kept alive)
+
+
+_fast: dict = {}
+
+
+def tensor_sig(t):
+    return (t.data_ptr(), t.shape, t.stride(), t.dtype, t.is_cuda)
+
+
+def fast_lookup(key):
+    """The entry prepared for ``key`` on the current stream of its device,
+    or None."""
+    ent = _fast.get(key)
+    if ent is None:
+        return None
+    if _raw_stream is not None:
+        stream = _raw_stream(ent.device)
+    else:
+        stream = torch.cuda.current_stream(ent.device).cuda_stream
+    return ent if stream == ent.stream else None
+
+
+def fast_store(key, ent):
+    if len(_fast) >= _FAST_MAX:
+        _fast.clear()
+    _fast[key] = ent
+
+
+def fast_run(ent, out_ptr=None):
+    """Launch a prepared entry (``out_ptr`` fills the output slot) and apply
+    the validation mode, as the full wrapper would."""
+    cur = torch.cuda.current_device()
+    if cur != ent.device:
+        torch.cuda.set_device(ent.device)
+    try:
+        for fn, args, slot, what in ent.calls:
+            if slot >= 0:
+                args = list(args)
+                args[slot] = out_ptr
+            _lib.check_status(fn(*args), what)
+    finally:
+        if cur != ent.device:
+            torch.cuda.set_device(cur)
+    if validation_mode() == "sync":
+        raise_for_bits(read_and_clear(_words[ent.device]))
+
+
+def fast_clear():
+    _fast.clear()

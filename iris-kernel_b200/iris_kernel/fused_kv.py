@@ -112,6 +112,13 @@ def fused_rope_int4_paged_append(
     """RoPE(K), group-32 INT4 quantisation of K and V, low-nibble-first
     packing and paged append, in place.  Tokens with ``slot_mapping < 0`` are
     skipped; untouched slots stay byte-identical."""
+    sig = _runtime.tensor_sig
+    sig_key = ("int4_append", sig(key), sig(value), sig(positions), sig(slot_mapping), sig(cos_cache), sig(sin_cache),
+           sig(k_data), sig(v_data), sig(k_scale), sig(v_scale), rotary_dim, group_size, page_size)
+    ent = _runtime.fast_lookup(sig_key)
+    if ent is not None:  # the same signature passed every host check before
+        _runtime.fast_run(ent)
+        return
     if not _runtime.cuda_available():
         raise RuntimeError("Iris fused kernels require CUDA")
     num_tokens, num_kv_heads, head_dim, num_pages = _check_append_args(
@@ -124,23 +131,26 @@ def fused_rope_int4_paged_append(
     with torch.cuda.device(device):
         stream = _runtime.stream_ptr(device)
         word = _runtime.error_word(device)
+        calls, keep = [], [word]
         if num_tokens > _lib.APPEND_INLINE_CHECK_TOKENS:  # smaller batches are checked by the append itself
             ws_bytes = _lib.lib.iris_b200_append_check_workspace_bytes(num_pages, page_size)
             ws = _runtime.scratch(device, stream, "append_check", max(ws_bytes, 4))
-            _lib.check_status(
-                _lib.lib.iris_b200_append_check(positions.data_ptr(), slot_mapping.data_ptr(), num_tokens,
-                                                cos_cache.shape[0], num_pages, page_size, ws.data_ptr(),
-                                                ws.numel(), word.data_ptr(), stream),
-                "iris_b200_append_check")
+            keep.append(ws)
+            calls.append((_lib.lib.iris_b200_append_check,
+                          [positions.data_ptr(), slot_mapping.data_ptr(), num_tokens, cos_cache.shape[0], num_pages,
+                           page_size, ws.data_ptr(), ws.numel(), word.data_ptr(), stream], -1,
+                          "iris_b200_append_check"))
         # the append kernel writes nothing if the check recorded an error, so
         # one host read after the launches keeps "raise before writing"
-        _lib.check_status(
-            _lib.lib.iris_b200_rope_int4_paged_append(
-                key.data_ptr(), value.data_ptr(), positions.data_ptr(), slot_mapping.data_ptr(),
-                cos_cache.data_ptr(), sin_cache.data_ptr(), k_data.data_ptr(), v_data.data_ptr(),
-                k_scale.data_ptr(), v_scale.data_ptr(), num_tokens, num_kv_heads, head_dim, cos_cache.shape[0],
-                num_pages, page_size, word.data_ptr(), stream),
-            "iris_b200_rope_int4_paged_append")
+        calls.append((_lib.lib.iris_b200_rope_int4_paged_append,
+                      [key.data_ptr(), value.data_ptr(), positions.data_ptr(), slot_mapping.data_ptr(),
+                       cos_cache.data_ptr(), sin_cache.data_ptr(), k_data.data_ptr(), v_data.data_ptr(),
+                       k_scale.data_ptr(), v_scale.data_ptr(), num_tokens, num_kv_heads, head_dim,
+                       cos_cache.shape[0], num_pages, page_size, word.data_ptr(), stream], -1,
+                      "iris_b200_rope_int4_paged_append"))
+        for fn, args, _, what in calls:
+            _lib.check_status(fn(*args), what)
+        _runtime.fast_store(sig_key, _runtime.FastEntry(calls, device.index, stream, keep))
         if _runtime.validation_mode() == "sync":
             _runtime.raise_for_bits(_runtime.read_and_clear(word))
 

@@ -1,7 +1,9 @@
 """DecodeStep (append + decode captured in one CUDA graph) equals the same
-two calls made eagerly: identical cache bytes and output, over several steps
-that append one token per sequence and extend the lengths; a rejected
-append inside the graph is reported by check=True and writes nothing."""
+two calls made eagerly (identical cache bytes and output) and the CPU
+oracle (cache bytes bit-exact, output within the decode tolerance), over
+several steps that append one token per sequence and extend the lengths; a
+rejected append inside the graph is reported by check=True and writes
+nothing."""
 import numpy as np
 import pytest
 import torch
@@ -9,7 +11,7 @@ import torch
 import math
 
 import cases
-from _refs import to_dev
+from _refs import assert_decode_close, to_dev
 from oracle import iris_oracle as orc
 
 pytestmark = pytest.mark.gpu
@@ -45,6 +47,8 @@ def test_graph_step_equals_eager_calls():
     Hkv = ta["k_data"].shape[2]
     for t in (ta, tb):  # the prefill, written the same way on both
         fused_rope_int4_paged_append(*[t[k] for k in cases.APPEND_KEYS], rotary_dim=D, page_size=16)
+    oc = {k: (v.copy() if isinstance(v, np.ndarray) else v) for k, v in c.items()}  # the oracle's copy
+    orc.append(**{k: oc[k] for k in cases.APPEND_KEYS}, rotary_dim=D, group_size=32, page_size=16)
     step = DecodeStep(ta["k_data"], ta["v_data"], ta["k_scale"], ta["v_scale"], ta["block_table"], ta["seq_lens"],
                       ta["cos_cache"], ta["sin_cache"], num_q_heads=Hq, new_tokens=B, rotary_dim=D)
     g = torch.Generator(device="cuda").manual_seed(7)
@@ -66,6 +70,16 @@ def test_graph_step_equals_eager_calls():
         assert torch.equal(out_graph, out_eager)
         for k_ in ("k_data", "v_data", "k_scale", "v_scale"):
             assert torch.equal(ta[k_], tb[k_])
+        # the oracle, on the same step inputs
+        oc["seq_lens"] = oc["seq_lens"] + 1
+        orc.append(k.cpu().numpy(), v.cpu().numpy(), pos.cpu().numpy(), slots.cpu().numpy(), oc["cos_cache"],
+                   oc["sin_cache"], oc["k_data"], oc["v_data"], oc["k_scale"], oc["v_scale"], rotary_dim=D,
+                   group_size=32, page_size=16)
+        for k_ in ("k_data", "v_data", "k_scale", "v_scale"):
+            assert ta[k_].cpu().numpy().tobytes() == oc[k_].tobytes(), k_
+        ref = orc.decode_attention(q.cpu().numpy(), oc["k_data"], oc["v_data"], oc["k_scale"], oc["v_scale"],
+                                   oc["block_table"], oc["seq_lens"])
+        assert_decode_close(out_graph, ref)
 
 
 def test_graph_step_reports_a_rejected_append():

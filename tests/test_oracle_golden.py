@@ -196,3 +196,24 @@ def test_merge_of_split_partials_equals_full():
         parts_l.append(l)
     merged = orc.merge_partials(np.stack(parts_o), np.stack(parts_l))
     np.testing.assert_allclose(merged[0], full[b], atol=1e-5, rtol=1e-5)
+
+
+@pytest.mark.parametrize("make", [cases.attention_ref_case, cases.config1], ids=["reference_fixture", "config1"])
+def test_int4_oracle_tracks_fp16_oracle(make):
+    """The reference's quality gate (tests/test_attention.py:199-232: mean
+    cosine > 0.97 and RMSE < 0.20 between the INT4 and the matched FP16
+    decode over the same keys and values) holds for the oracle's INT4 and FP16
+    restatements: the same K/V appended once quantised, once in fp16."""
+    c = _run_append(make())
+    NP, P, Hkv, _ = c["k_data"].shape
+    D = c["query"].shape[2]
+    kc = np.zeros((NP, P, Hkv, D), np.float16)
+    vc = np.zeros_like(kc)
+    orc.append_fp16(c["key"], c["value"], c["positions"], c["slot_mapping"], c["cos_cache"], c["sin_cache"], kc, vc,
+                    rotary_dim=D, page_size=P)
+    a = orc.decode_attention(*[c[k] for k in cases.DECODE_KEYS]).astype(np.float16).astype(np.float64)
+    b = orc.decode_attention_fp16(c["query"], kc, vc, c["block_table"], c["seq_lens"]).astype(np.float16)
+    a, b = a.reshape(-1, D), b.astype(np.float64).reshape(-1, D)
+    cosine = np.mean(np.sum(a * b, -1) / (np.linalg.norm(a, axis=-1) * np.linalg.norm(b, axis=-1)))
+    rmse = np.sqrt(np.mean((a - b) ** 2))
+    assert cosine > 0.97 and rmse < 0.20, (cosine, rmse)

@@ -6,16 +6,17 @@ keeps its scratch in a static array inside the library.
 
 Called through the C ABI twice in a row on different inputs (the second call
 reuses the scratch the first one left), each output must match the regular
-entry point's (which gets a workspace from the caller) within the decode
-tolerance of the other tests.  Collected last (file name) so that a run that
-stops at the first failure has run every other test first; it also passes
-alone in a fresh process."""
+entry point's (which gets a workspace from the caller) and the FP32 oracle
+within the decode tolerance of the other tests.  Collected last (file name)
+so that a run that stops at the first failure has run every other test
+first; it also passes alone in a fresh process."""
 import numpy as np
 import pytest
 import torch
 
 import cases
 from _refs import assert_decode_close, to_dev
+from oracle import iris_oracle as orc
 
 pytestmark = pytest.mark.gpu
 
@@ -64,19 +65,35 @@ def test_noalloc_decode_matches_regular_entry_point_twice():
         got = _noalloc(lib, t)
         ref = _regular(lib, t)
         assert_decode_close(got, ref)
+        assert_decode_close(got, orc.decode_attention(*[c[k] for k in cases.DECODE_KEYS]))
     # and once more on the first input after the second call changed the scratch
     t = to_dev(first, cases.DECODE_KEYS)
-    assert_decode_close(_noalloc(lib, t), _regular(lib, t))
+    got = _noalloc(lib, t)
+    assert_decode_close(got, _regular(lib, t))
+    assert_decode_close(got, orc.decode_attention(*[first[k] for k in cases.DECODE_KEYS]))
+
+
+def test_noalloc_serves_small_mqa_problems():
+    """The scratch a call needs is sized by its problem (its page count caps
+    the split-KV ranges), so a short MQA decode at D=128, whose SM-derived
+    worst case exceeds the array, still runs."""
+    from iris_kernel import _lib
+
+    lib = _lib.lib
+    assert lib.iris_b200_decode_workspace_bytes(1, 16, 1, 128, 0) > _lib.DECODE_NOALLOC_SCRATCH_BYTES
+    c = cases.decode_random(seed=74, B=1, Hq=16, Hkv=1, D=128, lens=[64])
+    t = to_dev(c, cases.DECODE_KEYS)
+    got = _noalloc(lib, t)
+    assert_decode_close(got, orc.decode_attention(*[c[k] for k in cases.DECODE_KEYS]))
 
 
 def test_noalloc_rejects_problems_larger_than_its_scratch():
     from iris_kernel import _lib
 
     lib = _lib.lib
-    # MQA with 16 query heads at D=128 needs more split-KV records than the array holds
-    need = lib.iris_b200_decode_workspace_bytes(1, 16, 1, 128, 0)
-    assert need > _lib.DECODE_NOALLOC_SCRATCH_BYTES
-    c = cases.decode_random(seed=73, B=1, Hq=16, Hkv=1, D=128, lens=[64])
+    # MQA with 16 query heads at D=128 over a block table of 8404 columns may
+    # use ~2100 split-KV ranges of 16 KB of records each: more than the array
+    c = cases.decode_random(seed=73, B=1, Hq=16, Hkv=1, D=128, lens=[64], extra_cols=8400)
     t = to_dev(c, cases.DECODE_KEYS)
     out = torch.full_like(t["query"], float("nan"))
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
