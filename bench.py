@@ -511,6 +511,82 @@ def cpu_baseline_sample(seconds_budget=15.0):
                       f"{dt:.1f} s", "cpu_model": _cpu_model()}
 
 
+TILELANG_APPEND_UNAVAILABLE = ("unavailable: the image's tilelang 0.1.9 cannot trace it (fused_kv.py:562 calls "
+                               "T.round(..., rounding_mode=...), which 0.1.9 lacks; the reference pins tilelang>=0.1.13)")
+
+
+def run_tilelang(args):
+    """The reference's own GPU decode kernel, _int4_paged_decode_attention
+    (fused_attention.py:11-220, TileLang, JIT-compiled here by the image's
+    tilelang) on config 2, loaded by file from the unmodified install in
+    baseline/_ref.  Prints one JSON line: the kernel's time replayed from a
+    CUDA graph, the public wrapper's time (its per-call host checks
+    included), and its max error against an FP32 dequantise-then-attend
+    reference on two sequences."""
+    path = os.path.join(ROOT, "baseline", "_ref", "iris_kernel", "fused_attention.py")
+    if not os.path.isfile(path):
+        print(json.dumps({"impl": "tilelang", "unavailable": "reference not installed in baseline/_ref"}), flush=True)
+        return
+    res = {"impl": "tilelang", "kernel": "_int4_paged_decode_attention (reference, TileLang JIT)",
+           "append": TILELANG_APPEND_UNAVAILABLE}
+    try:
+        import tilelang
+
+        res["tilelang"] = tilelang.__version__
+        t0 = time.time()
+        spec = importlib.util.spec_from_file_location("_iris_reference_fused_attention", path)
+        fa = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(fa)
+        dev = torch.device("cuda", 0)
+        g = torch.Generator(device=dev).manual_seed(0)
+        pool = B * (L // P + 1)
+        kd = torch.randint(0, 256, (pool, P, HKV, D // 2), dtype=torch.uint8, device=dev, generator=g)
+        vd = torch.randint(0, 256, (pool, P, HKV, D // 2), dtype=torch.uint8, device=dev, generator=g)
+        ks = (torch.rand((pool, P, HKV, D // G), device=dev, generator=g) * 0.1 + 0.01).half()
+        vs = (torch.rand((pool, P, HKV, D // G), device=dev, generator=g) * 0.1 + 0.01).half()
+        bt = torch.randperm(pool, device=dev, generator=g).int().view(B, L // P + 1).contiguous()
+        lens = torch.full((B,), L, dtype=torch.int32, device=dev)
+        q = torch.randn(B, HQ, D, device=dev, generator=g).half()
+        out = torch.empty_like(q)
+        fa.fused_int4_paged_decode_attention(q, kd, vd, ks, vs, bt, lens, out)  # JIT compile
+        torch.cuda.synchronize()
+        res["jit_s"] = round(time.time() - t0, 1)
+        err = 0.0
+        for b in range(2):
+            o, _ = _fp32_partial(q[b], kd, vd, ks, vs, bt[b], L, HQ)
+            err = max(err, float((out[b].float() - o).abs().max()))
+        res["max_abs_err_vs_fp32"] = err
+        raw = lambda: fa._int4_paged_decode_attention(q, kd, vd, ks, vs, bt, lens, out, D, P, G, 16, 32, 128, 0.0)
+        gr = graph_of(raw, dev)
+        n = max(10, min(args.steps, 50))
+        us = timed(gr.replay, n, dev, None, 3) / n * 1e3
+        res["decode_us"] = us
+        res["decode_tbs"] = DECODE_BYTES / (us * 1e-6) / 1e12
+        n_api = 5
+        res["api_us"] = timed(lambda: fa.fused_int4_paged_decode_attention(q, kd, vd, ks, vs, bt, lens, out), n_api,
+                              dev, None, 2) / n_api * 1e3
+        del gr
+    except Exception as e:  # report why, as the line's result
+        res["unavailable"] = f"{type(e).__name__}: {str(e)[:300]}"
+    print(json.dumps(res), flush=True)
+
+
+def tilelang_leg(args, dec_us):
+    """Runs run_tilelang in a child process (the JIT and the reference's
+    modules stay out of this process) and returns its result."""
+    try:
+        out = subprocess.run([sys.executable, os.path.abspath(__file__), "--impl", "tilelang", "--steps",
+                              str(args.steps)], capture_output=True, text=True, timeout=420)
+        lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
+        res = json.loads(lines[-1]) if lines else {"unavailable": (out.stderr or out.stdout)[-300:]}
+    except Exception as e:
+        res = {"unavailable": f"{type(e).__name__}: {str(e)[:200]}"}
+    res.pop("impl", None)
+    if "decode_us" in res:
+        res["ours_speedup"] = res["decode_us"] / dec_us
+    return res
+
+
 def run_reference(args, dist, rank, world):
     """The reference's CPU path on the host cores, rank 0 only: every step
     is a measured run of torch_eager_int4_paged_decode_attention over the
@@ -673,11 +749,14 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "tilelang"])
     ap.add_argument("--only", default="all", choices=["all", "c2", "c3", "c4", "c5a", "c5b", "f16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.impl == "tilelang":  # the reference's TileLang decode on one GPU (a child of the N=1 run)
+        run_tilelang(args)
+        return
     if args.impl == "reference":
         # host work only: no process group; under torchrun rank 0 alone runs it
         run_reference(args, None, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))
@@ -805,9 +884,11 @@ def main():
         del g_c3, c3
     iris_kernel.set_validation_mode("sync")
 
-    cpu = None
+    cpu, tl = None, None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and run("c2"):
         cpu = cpu_baseline_sample(seconds_budget=15.0)
+        torch.cuda.empty_cache()
+        tl = tilelang_leg(args, dec_us)
 
     if rank == 0:
         if not run("c2"):
@@ -847,6 +928,7 @@ def main():
                              "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic,
                              "kernel": "decode + combine (graph), per GPU"},
                 "cpu_baseline": cpu, "clocks": clocks, **{k: _round(v) for k, v in extra.items()},
+                "tilelang_ref": _round(tl) if tl is not None else None,
             }
             print(json.dumps(line), flush=True)
     if dist is not None:

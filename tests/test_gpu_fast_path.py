@@ -37,6 +37,8 @@ def test_repeat_decode_calls_match_the_oracle_and_each_other():
     assert_decode_close(other, orc.decode_attention(*[c[k] for k in cases.DECODE_KEYS], softmax_scale=0.2))
     # a changed argument that fails a host check still raises
     with pytest.raises(NotImplementedError):
+        fused_int4_paged_decode_attention(*args, group_size=16)
+    with pytest.raises(ValueError):  # the cache's page size no longer matches
         fused_int4_paged_decode_attention(*args, page_size=32)
 
 
