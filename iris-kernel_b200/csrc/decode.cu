@@ -235,20 +235,37 @@ IRIS_DEV void load_query(WarpState<D, NT>& st, const __half* __restrict__ q_seq,
   }
 }
 
-// Lane offsets for the four 8x8 matrices of one ldmatrix.x4 over a swizzled
-// [16][D/2] tile: matrix (l>>3) covers token rows 8*((l>>3)&1).. and 16-byte
-// segment 2*i + (l>>4).
-template <int D>
-IRIS_DEV uint32_t tile_lane_offset(int lane, int i) {
-  const int mat = lane >> 3;
-  const int row = (lane & 7) + 8 * (mat & 1);
-  const int seg = 2 * i + (mat >> 1);
-  if constexpr (D == 128) {
-    return row * 64 + ((seg ^ ((row >> 1) & 3)) * 16);  // TMA SWIZZLE_64B
-  } else {
-    return row * 32 + ((seg ^ ((row >> 2) & 1)) * 16);  // TMA SWIZZLE_32B
+// Shared-memory layout of a stage's K (or V) tiles for the CTA's block of
+// HB KV heads, and each lane's ldmatrix.x4 address in it.  The four 8x8
+// matrices of one ldmatrix.x4 cover token rows 8*((l>>3)&1).. and 16-byte
+// segments 2*i + (l>>4) of head g's D/2-byte row.
+//  * R128 = false: one [16 tokens][D/2 bytes] tile per head, swizzled by the
+//    tensor map's 64-byte (D = 128) or 32-byte (D = 64) pattern.
+//  * R128 = true: one [16 tokens][128 bytes] tile per kRowHeads = 256 / D
+//    adjacent heads (a 128-byte row holds one token of all of them, as the
+//    cache stores it), swizzled by the 128-byte pattern: 16-byte chunk c of
+//    row r sits at chunk c ^ (r & 7).  Whole 128-byte rows make the TMA's
+//    transactions whole lines.
+// lane_off(lane, g) is the offset of segment pair 0 of head g; the segment-
+// pair bit is disjoint from the others, so pair i is at lane_off ^ (32 * i)
+// (also after adding a 1-KB aligned stage base).
+template <int D, bool R128>
+struct KvTiles {
+  static constexpr int kTile = kPage * D / 2;  // bytes of one head per page
+  static constexpr int kRowHeads = 256 / D;    // heads per 128-byte row (R128)
+  IRIS_DEV static uint32_t lane_off(int lane, int g) {
+    const int mat = lane >> 3;
+    const int row = (lane & 7) + 8 * (mat & 1);
+    if constexpr (R128) {
+      const uint32_t unit = static_cast<uint32_t>(g / kRowHeads) * (kRowHeads * kTile);
+      const int chunk = (g % kRowHeads) * (D / 32) + (mat >> 1);
+      return unit + row * 128 + ((chunk ^ (lane & 7)) << 4);
+    } else {
+      const int sw = D == 128 ? ((row >> 1) & 3) : ((row >> 2) & 1);  // TMA SWIZZLE_64B / SWIZZLE_32B
+      return static_cast<uint32_t>(g) * kTile + row * (D / 2) + (((mat >> 1) ^ sw) << 4);
+    }
   }
-}
+};
 
 // One page (16 tokens) of one KV head.
 // Scores of one page (16 tokens) for this warp's KV head:
@@ -265,7 +282,7 @@ IRIS_DEV void page_scores(const WarpState<D, NT>& st, uint32_t ktile, uint32_t k
 #pragma unroll
   for (int i = 0; i < G / 2; ++i) {
     uint32_t r[4];
-    ldmatrix_x4(r, ktile + tile_lane_offset<D>(lane, i));
+    ldmatrix_x4(r, ktile ^ (32u * i));
     kw[2 * i][0] = r[0];
     kw[2 * i][1] = r[1];
     kw[2 * i + 1][0] = r[2];
@@ -354,7 +371,7 @@ IRIS_DEV void page_pv(WarpState<D, NT>& st, uint32_t vtile, uint32_t vsc, int sc
 #pragma unroll
   for (int i = 0; i < G / 2; ++i) {
     uint32_t r[4];
-    ldmatrix_x4_trans(r, vtile + tile_lane_offset<D>(lane, i));
+    ldmatrix_x4_trans(r, vtile ^ (32u * i));
     // r[0] = (tokens 2t,2t+1; group 2i), r[1] = (tokens 2t+8,2t+9; group 2i),
     // r[2], r[3] likewise for group 2i+1
 #pragma unroll
@@ -503,10 +520,14 @@ IRIS_DEV void finish_piece(const DecodeParams& p, WarpState<D, NT>& st, int b, i
 // How a stage's tiles are fetched: the INT4 cache (4-D box per tensor plus
 // the page's two scale blocks) or the FP16 cache (4-D box at D = 64, 5-D box
 // of two 128-byte halves per row at D = 128; no scales).
+// kRowHeads: heads per box row (1: one head's D/2 bytes per row; 256 / D:
+// 128-byte rows of kRowHeads heads), so the box's third coordinate is the
+// first head / kRowHeads.
+template <int kRowHeads>
 struct Int4Copy {
   static constexpr bool kScales = true;
   IRIS_DEV static void load(void* dst, const CUtensorMap* m, int head0, int pid, uint64_t* bar) {
-    tma_load_4d(dst, m, 0, 0, head0, pid, bar);
+    tma_load_4d(dst, m, 0, 0, head0 / kRowHeads, pid, bar);
   }
 };
 template <int kDims>
@@ -603,7 +624,7 @@ IRIS_DEV void run_producer(const CUtensorMap* kmap_p, const CUtensorMap* vmap_p,
   }
 }
 
-template <int D, int NT>
+template <int D, int NT, bool R128>
 __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ CUtensorMap kmap,
                                                         const __grid_constant__ CUtensorMap vmap,
                                                         const DecodeParams p) {
@@ -643,8 +664,9 @@ __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ CUtensorM
   const uint32_t full_u32 = smem_u32(full), empty_u32 = smem_u32(empty);
 
   if (warp == HB) {
-    run_producer<Int4Copy, C::kTileBytes>(&kmap, &vmap, p, smem, stage_bytes, S, HB, hblk, u0, u1, b_first, ps_first,
-                                          full, full_u32, empty_u32, scale_block, lane);
+    run_producer<Int4Copy<R128 ? 256 / D : 1>, C::kTileBytes>(&kmap, &vmap, p, smem, stage_bytes, S, HB, hblk, u0,
+                                                              u1, b_first, ps_first, full, full_u32, empty_u32,
+                                                              scale_block, lane);
     return;
   }
 
@@ -653,7 +675,8 @@ __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ CUtensorM
   WarpState<D, NT> st;
   const uint32_t ring = smem_u32(smem);
   // this warp's tiles and scale columns, relative to a stage's base
-  const uint32_t k_off = warp * C::kTileBytes, v_off = (HB + warp) * C::kTileBytes;
+  // this lane's ldmatrix addresses of the warp's head, relative to a stage's base
+  const uint32_t k_off = KvTiles<D, R128>::lane_off(lane, warp), v_off = HB * C::kTileBytes + k_off;
   const uint32_t ks_off = 2 * HB * C::kTileBytes + kvh * C::kGroups * 2;
   const uint32_t vs_off = ks_off + scale_block;
   const int scale_stride = p.hkv * C::kGroups * 2;
@@ -817,10 +840,9 @@ IRIS_DEV void pair_load_query(PairState<D>& st, const __half* __restrict__ q_seq
 // row address for head h's (masked) query tile, XOR 64*i selecting k-steps
 // 2i, 2i+1; ksc: the lane's head's column in the page's K scale block.
 template <int D, int HP>
-IRIS_DEV void pair_page_scores(const PairState<D>& st, uint32_t ktile0, const uint32_t (&qaddr)[HP], uint32_t ksc,
-                               int scale_stride, int lane, float (&s)[4]) {
+IRIS_DEV void pair_page_scores(const PairState<D>& st, uint32_t stage, const uint32_t (&klane)[HP],
+                               const uint32_t (&qaddr)[HP], uint32_t ksc, int scale_stride, int lane, float (&s)[4]) {
   constexpr int G = D / 32;
-  constexpr int kTile = kPage * D / 2;
   const int g8 = lane >> 2;
   float ks[2][G];
 #pragma unroll
@@ -843,7 +865,7 @@ IRIS_DEV void pair_page_scores(const PairState<D>& st, uint32_t ktile0, const ui
 #pragma unroll
     for (int h = 0; h < HP; ++h) {
       uint32_t kr[4];
-      ldmatrix_x4(kr, ktile0 + h * kTile + tile_lane_offset<D>(lane, i));
+      ldmatrix_x4(kr, (stage + klane[h]) ^ (32u * i));
 #pragma unroll
       for (int gg = 0; gg < 2; ++gg) {
         uint32_t qb[4];  // (b0, b1) of k-steps 2g, 2g+1 for head h
@@ -884,11 +906,10 @@ IRIS_DEV void pair_page_scores(const PairState<D>& st, uint32_t ktile0, const ui
 // B-operand head (column g8) in the V scale block; tokens >= `valid` get a
 // zero V scale when MASK.
 template <int D, int HP, bool MASK>
-IRIS_DEV void pair_page_pv(PairState<D>& st, uint32_t vtile0, uint32_t vsc, int scale_stride, int valid,
-                           const float (&p)[4], int lane) {
+IRIS_DEV void pair_page_pv(PairState<D>& st, uint32_t vstage, const uint32_t (&klane)[HP], uint32_t vsc,
+                           int scale_stride, int valid, const float (&p)[4], int lane) {
   constexpr int G = D / 32;
   constexpr int CW = 8 / HP;
-  constexpr int kTile = kPage * D / 2;
   const int t = lane & 3;
   const int hb = (lane >> 2) / CW;  // head of this lane's B column
   uint32_t sv01[G], sv89[G];
@@ -924,7 +945,7 @@ IRIS_DEV void pair_page_pv(PairState<D>& st, uint32_t vtile0, uint32_t vsc, int 
 #pragma unroll
     for (int i = 0; i < G / 2; ++i) {
       uint32_t r[4];
-      ldmatrix_x4_trans(r, vtile0 + h * kTile + tile_lane_offset<D>(lane, i));
+      ldmatrix_x4_trans(r, (vstage + klane[h]) ^ (32u * i));
 #pragma unroll
       for (int gg = 0; gg < 2; ++gg) {
         const int g = 2 * i + gg;
@@ -950,12 +971,12 @@ IRIS_DEV void pair_page_pv(PairState<D>& st, uint32_t vtile0, uint32_t vsc, int 
 // max reduction and the rescale are skipped.  `first` marks a piece's first
 // page: m then starts at that page's maxima (O and l are still zero).
 template <int D, int HP, bool MASK>
-IRIS_DEV void pair_process_page(PairState<D>& st, uint32_t base, uint32_t k_off, uint32_t v_off,
+IRIS_DEV void pair_process_page(PairState<D>& st, uint32_t base, const uint32_t (&klane)[HP], uint32_t v_off,
                                  const uint32_t (&qaddr)[HP], uint32_t ks_off, uint32_t vs_off, int scale_stride,
                                  int valid, float scale_log2, bool first, int lane) {
   const int g8 = lane >> 2;
   float s[4];
-  pair_page_scores<D, HP>(st, base + k_off, qaddr, base + ks_off, scale_stride, lane, s);
+  pair_page_scores<D, HP>(st, base, klane, qaddr, base + ks_off, scale_stride, lane, s);
   float y[4];
   y[0] = fmaf(s[0], scale_log2, -st.m[0]);
   y[1] = fmaf(s[1], scale_log2, -st.m[1]);
@@ -998,7 +1019,7 @@ IRIS_DEV void pair_process_page(PairState<D>& st, uint32_t base, uint32_t k_off,
   for (int k = 0; k < 4; ++k) pr[k] = ex2(y[k]);  // ex2(-inf) = 0 for masked tokens
   st.l[0] += pr[0] + pr[2];
   st.l[1] += pr[1] + pr[3];
-  pair_page_pv<D, HP, MASK>(st, base + v_off, base + vs_off, scale_stride, valid, pr, lane);
+  pair_page_pv<D, HP, MASK>(st, base + v_off, klane, base + vs_off, scale_stride, valid, pr, lane);
 }
 
 // Finish a (sequence piece, head group): column c of the fragments is query
@@ -1053,7 +1074,7 @@ IRIS_DEV void pair_finish_piece(const DecodeParams& p, PairState<D>& st, int b, 
 // Decode CTA with HB/HP consumer warps of HP heads each + 1 producer warp.
 // Shared memory: the stage ring, the full/empty barriers, a 256-byte zero
 // block, then one 2*8*D-byte query tile per consumer warp.
-template <int D, int HP>
+template <int D, int HP, bool R128>
 __global__ void __maxnreg__(128) decode_pair_kernel(const __grid_constant__ CUtensorMap kmap,
                                                              const __grid_constant__ CUtensorMap vmap,
                                                              const DecodeParams p) {
@@ -1098,8 +1119,9 @@ __global__ void __maxnreg__(128) decode_pair_kernel(const __grid_constant__ CUte
   const uint32_t full_u32 = smem_u32(full), empty_u32 = smem_u32(empty);
 
   if (warp == NW) {
-    run_producer<Int4Copy, C::kTileBytes>(&kmap, &vmap, p, smem, stage_bytes, S, HB, hblk, u0, u1, b_first, ps_first,
-                                          full, full_u32, empty_u32, scale_block, lane);
+    run_producer<Int4Copy<R128 ? 256 / D : 1>, C::kTileBytes>(&kmap, &vmap, p, smem, stage_bytes, S, HB, hblk, u0,
+                                                              u1, b_first, ps_first, full, full_u32, empty_u32,
+                                                              scale_block, lane);
     return;
   }
 
@@ -1118,7 +1140,12 @@ __global__ void __maxnreg__(128) decode_pair_kernel(const __grid_constant__ CUte
     for (int h = 0; h < HP; ++h)
       qaddr[h] = (row / CW == h ? qtile + row * (2 * D) : smem_u32(zero_blk)) | (x << 4);
   }
-  const uint32_t k_off = warp * HP * C::kTileBytes, v_off = (HB + warp * HP) * C::kTileBytes;
+  // this lane's ldmatrix addresses of the warp's heads, relative to a stage's K
+  // region (the V region follows it at HB tiles)
+  uint32_t klane[HP];
+#pragma unroll
+  for (int h = 0; h < HP; ++h) klane[h] = KvTiles<D, R128>::lane_off(lane, warp * HP + h);
+  const uint32_t v_off = HB * C::kTileBytes;
   const uint32_t ks_off = 2 * HB * C::kTileBytes + (kv0 + (2 * t) / CW) * C::kGroups * 2;
   const uint32_t vs_off = 2 * HB * C::kTileBytes + scale_block + (kv0 + g8 / CW) * C::kGroups * 2;
   const int scale_stride = p.hkv * C::kGroups * 2;
@@ -1144,10 +1171,10 @@ __global__ void __maxnreg__(128) decode_pair_kernel(const __grid_constant__ CUte
     for (int64_t left = hi - u; left > 0; --left) {
       if (!mbar_wait_bounded(full_u32 + 8 * s, ph, p.err)) return;
       if (valid >= kPage)
-        pair_process_page<D, HP, false>(st, stage, k_off, v_off, qaddr, ks_off, vs_off, scale_stride, valid,
+        pair_process_page<D, HP, false>(st, stage, klane, v_off, qaddr, ks_off, vs_off, scale_stride, valid,
                                         p.scale_log2, first, lane);
       else
-        pair_process_page<D, HP, true>(st, stage, k_off, v_off, qaddr, ks_off, vs_off, scale_stride, valid,
+        pair_process_page<D, HP, true>(st, stage, klane, v_off, qaddr, ks_off, vs_off, scale_stride, valid,
                                        p.scale_log2, first, lane);
       __syncwarp();
       if (lane == 0) mbar_arrive(empty_u32 + 8 * s);
@@ -1611,9 +1638,25 @@ EncodeTiledFn encode_fn() {
 // box of (D/2, 16, hb, 1) lands as hb per-head [16][D/2] tiles, swizzled so
 // that ldmatrix reads them without bank conflicts: one copy per page per
 // tensor for the whole head block.
-bool make_kv_map(CUtensorMap* map, const void* base, int D, int hkv, int hb, int64_t num_pages) {
+//
+// r128: the view (128 bytes, 16 tokens, Hkv / RH units, pages) with RH =
+// 256 / D adjacent heads per 128-byte row and the 128-byte swizzle; a box of
+// (128, 16, hb / RH, 1) lands as hb / RH tiles [16][128 B].
+bool make_kv_map(CUtensorMap* map, const void* base, int D, int hkv, int hb, int64_t num_pages, bool r128) {
   EncodeTiledFn enc = encode_fn();
   if (enc == nullptr) return false;
+  if (r128) {
+    const int rh = 256 / D;
+    const cuuint64_t dims[4] = {128u, static_cast<cuuint64_t>(kPage), static_cast<cuuint64_t>(hkv / rh),
+                                static_cast<cuuint64_t>(num_pages)};
+    const cuuint64_t strides[3] = {static_cast<cuuint64_t>(hkv) * (D / 2), 128u,
+                                   static_cast<cuuint64_t>(hkv) * (D / 2) * kPage};
+    const cuuint32_t box[4] = {128u, static_cast<cuuint32_t>(kPage), static_cast<cuuint32_t>(hb / rh), 1u};
+    const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  }
   const cuuint64_t dims[4] = {static_cast<cuuint64_t>(D / 2), static_cast<cuuint64_t>(kPage),
                               static_cast<cuuint64_t>(hkv), static_cast<cuuint64_t>(num_pages)};
   const cuuint64_t strides[3] = {static_cast<cuuint64_t>(hkv) * (D / 2), static_cast<cuuint64_t>(D / 2),
@@ -1678,7 +1721,9 @@ bool cached_kv_map(CUtensorMap* map, int fmt, const void* base, int D, int hkv, 
       }
     }
   }
-  if (!(fmt == 0 ? make_kv_map(map, base, D, hkv, hb, num_pages) : make_fp16_map(map, base, D, hkv, hb, num_pages)))
+  // fmt: 0 INT4 one head per row, 2 INT4 128-byte rows, 1 FP16
+  if (!(fmt == 1 ? make_fp16_map(map, base, D, hkv, hb, num_pages)
+                 : make_kv_map(map, base, D, hkv, hb, num_pages, fmt == 2)))
     return false;
   std::lock_guard<std::mutex> lock(mu);
   Entry& e = cache[next];
@@ -1712,10 +1757,21 @@ int max_hb(int dflt) {
   return v ? v : dflt;
 }
 
+// 128-byte-row tiles unless IRIS_DECODE_R128=0 (the one-head-per-row form,
+// kept for comparison).
+bool use_r128() {
+  static const bool v = [] {
+    const char* e = getenv("IRIS_DECODE_R128");
+    return !(e && e[0] == '0');
+  }();
+  return v;
+}
+
 // The CTA shape of one decode problem.
 struct Plan {
   DecodeKernelFn fn;
   int fp16;  // FP16 cache (decode_fp16_kernel): bigger tiles, no scale blocks
+  int r128;  // INT4 tiles of 128-byte rows (head blocks of whole rows of 256 / D heads)
   int hp;    // KV heads per consumer warp
   int hb;    // KV heads per CTA (one TMA box)
   int nw;    // consumer warps = hb / hp
@@ -1735,12 +1791,21 @@ Plan make_plan(int D, int qpk, int hkv) {
       break;
     }
   pl.nw = pl.hb / pl.hp;
+  pl.r128 = use_r128() && pl.hb % (256 / D) == 0;
   if (D == 128) {
-    pl.fn = pl.hp == 4 ? decode_pair_kernel<128, 4> : pl.hp == 2 ? decode_pair_kernel<128, 2>
-          : qpk <= 8   ? decode_kernel<128, 1>      : decode_kernel<128, 2>;
+    if (pl.r128)
+      pl.fn = pl.hp == 4 ? decode_pair_kernel<128, 4, true> : pl.hp == 2 ? decode_pair_kernel<128, 2, true>
+            : qpk <= 8   ? decode_kernel<128, 1, true>      : decode_kernel<128, 2, true>;
+    else
+      pl.fn = pl.hp == 4 ? decode_pair_kernel<128, 4, false> : pl.hp == 2 ? decode_pair_kernel<128, 2, false>
+            : qpk <= 8   ? decode_kernel<128, 1, false>      : decode_kernel<128, 2, false>;
   } else {
-    pl.fn = pl.hp == 4 ? decode_pair_kernel<64, 4> : pl.hp == 2 ? decode_pair_kernel<64, 2>
-          : qpk <= 8   ? decode_kernel<64, 1>      : decode_kernel<64, 2>;
+    if (pl.r128)
+      pl.fn = pl.hp == 4 ? decode_pair_kernel<64, 4, true> : pl.hp == 2 ? decode_pair_kernel<64, 2, true>
+            : qpk <= 8   ? decode_kernel<64, 1, true>      : decode_kernel<64, 2, true>;
+    else
+      pl.fn = pl.hp == 4 ? decode_pair_kernel<64, 4, false> : pl.hp == 2 ? decode_pair_kernel<64, 2, false>
+            : qpk <= 8   ? decode_kernel<64, 1, false>      : decode_kernel<64, 2, false>;
   }
   return pl;
 }
@@ -1754,6 +1819,7 @@ struct LaunchShape {
 Plan make_plan_fp16(int D, int qpk, int hkv) {
   Plan pl;
   pl.fp16 = 1;
+  pl.r128 = 0;
   pl.hp = 1;
   pl.pair = 0;
   const int cap = max_hb(4);
@@ -2012,7 +2078,7 @@ static int decode_entry(bool fp16, const void* query, const void* k_data, const 
 
   CUtensorMap km, vm;
   const Plan plan = fp16 ? make_plan_fp16(head_dim, qpk, num_kv_heads) : make_plan(head_dim, qpk, num_kv_heads);
-  const int fmt = fp16 ? 1 : 0;
+  const int fmt = fp16 ? 1 : (plan.r128 ? 2 : 0);
   if (!cached_kv_map(&km, fmt, k_data, head_dim, num_kv_heads, plan.hb, num_pages) ||
       !cached_kv_map(&vm, fmt, v_data, head_dim, num_kv_heads, plan.hb, num_pages)) {
     snprintf(iris::g_last_error, sizeof(iris::g_last_error), "cuTensorMapEncodeTiled failed (D=%d Hkv=%d pages=%lld)", head_dim,
