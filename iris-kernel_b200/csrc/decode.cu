@@ -78,6 +78,7 @@ struct DecodeParams {
   int32_t qpk;               // query heads per KV head
   int32_t stages;
   int32_t out_mode;
+  int32_t ranges;            // page ranges launched (the decode grid's y extent)
   float scale_log2;          // softmax_scale * log2(e)
 };
 
@@ -113,7 +114,101 @@ IRIS_DEV int32_t seq_pages(const DecodeParams& p, int b) {
   return np < p.max_pages ? np : p.max_pages;
 }
 
+// Batches of at most 32 * kPlanPerLane sequences: lane l takes sequences
+// [l*K, l*K + K), K = ceil(batch / 32), loads all their lengths at once (one
+// memory round trip instead of two dependent passes) and keeps the page
+// counts in registers for the prefix scan and for finding the range's first
+// sequence.
+constexpr int kPlanPerLane = 8;
+
+IRIS_DEV void plan_cta_regs(const DecodeParams& p, int r, int ranges, bool leader, int lane, CtaPlan* out) {
+  const int K = (p.batch + 31) / 32;
+  const int b0 = lane * K;
+  int32_t np[kPlanPerLane];
+#pragma unroll
+  for (int j = 0; j < kPlanPerLane; ++j) {
+    const int b = b0 + j;
+    np[j] = (j < K && b < p.batch) ? __ldg(p.seq_lens + b) : 0;
+  }
+  int32_t tot = 0;
+#pragma unroll
+  for (int j = 0; j < kPlanPerLane; ++j) {
+    const int b = b0 + j;
+    const int32_t L = np[j];
+    int32_t n = 0;
+    if (j < K && b < p.batch) {
+      if (L <= 0) {
+        if (leader) set_error(p.err, IRIS_ERR_SEQ_LEN);
+      } else {
+        n = (L + kPage - 1) / kPage;
+        if (n > p.max_pages) {
+          if (leader) set_error(p.err, IRIS_ERR_BLOCK_TABLE);
+          n = p.max_pages;
+        }
+      }
+    }
+    np[j] = n;
+    tot += n;
+  }
+  int32_t x = tot;  // inclusive scan of the lanes' totals
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  const int32_t excl = x - tot;
+  const int64_t U = __shfl_sync(0xffffffffu, x, 31);
+  if (leader) {
+    int32_t run = excl;
+#pragma unroll
+    for (int j = 0; j < kPlanPerLane; ++j) {
+      if (j < K && b0 + j < p.batch) const_cast<int32_t*>(p.prefix)[b0 + j] = run;
+      run += np[j];
+    }
+  }
+  int32_t R = 0;
+  if (U > 0) {
+    const int64_t want = (U + kMinPagesPerRange - 1) / kMinPagesPerRange;
+    R = static_cast<int32_t>(want < ranges ? want : ranges);
+  }
+  if (leader && lane == 0) {
+    const_cast<int32_t*>(p.prefix)[p.batch] = static_cast<int32_t>(U);
+    const_cast<int32_t*>(p.meta)[0] = static_cast<int32_t>(U);
+    const_cast<int32_t*>(p.meta)[1] = R;
+  }
+  int32_t bf = 0, psf = 0;
+  if (r < R) {
+    // the sequence holding page u0: the first b whose pages end past u0
+    const int64_t u0 = range_start(r, U, R);
+    const unsigned hit = __ballot_sync(0xffffffffu, static_cast<int64_t>(x) > u0);
+    const int i = __ffs(hit) - 1;
+    int32_t run = excl, mb = 0, mps = 0;
+    bool found = false;
+#pragma unroll
+    for (int j = 0; j < kPlanPerLane; ++j) {
+      if (!found && static_cast<int64_t>(run) + np[j] > u0) {
+        found = true;
+        mb = b0 + j;
+        mps = run;
+      }
+      run += np[j];
+    }
+    bf = __shfl_sync(0xffffffffu, mb, i);
+    psf = __shfl_sync(0xffffffffu, mps, i);
+  }
+  if (lane == 0) {
+    out->U = U;
+    out->R = R;
+    out->b_first = bf;
+    out->ps_first = psf;
+  }
+}
+
 IRIS_DEV void plan_cta(const DecodeParams& p, int r, int ranges, bool leader, int lane, CtaPlan* out) {
+  if (p.batch <= 32 * kPlanPerLane) {
+    plan_cta_regs(p, r, ranges, leader, lane, out);
+    return;
+  }
   int64_t U = 0;
   for (int base = 0; base < p.batch; base += 32) {
     const int b = base + lane;
@@ -1513,15 +1608,55 @@ __global__ void __maxnreg__(128) decode_fp16_kernel(const __grid_constant__ CUte
 constexpr int kCombineThreads = 256;
 constexpr int kCombineSplit = 4;  // CTAs per sequence, each a quarter of its (query head, 4 dims) items
 
+// Where sequence b's pages sit in the batch's concatenation, the total U and
+// the ranges R in use, recomputed from seq_lens exactly as the decode's plan
+// computes them (an input of the call, so this runs while the decode is
+// still working): warp 0 of the CTA, the result in shared memory.
+struct SeqSpan {
+  int64_t ps, pe, U;
+  int32_t R;
+};
+
+IRIS_DEV void combine_span(const DecodeParams& p, int b, int lane, SeqSpan* out) {
+  int64_t U = 0, ps = 0, pe = 0;
+  for (int base = 0; base < p.batch; base += 32) {
+    const int bb = base + lane;
+    int32_t np = bb < p.batch ? seq_pages(p, bb) : 0;
+    int32_t x = np;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (bb == b) {
+      ps = U + x - np;
+      pe = U + x;
+    }
+    U += __shfl_sync(0xffffffffu, x, 31);
+  }
+  const int src = b & 31;
+  ps = __shfl_sync(0xffffffffu, ps, src);
+  pe = __shfl_sync(0xffffffffu, pe, src);
+  int32_t R = 0;
+  if (U > 0) {
+    const int64_t want = (U + kMinPagesPerRange - 1) / kMinPagesPerRange;
+    R = static_cast<int32_t>(want < p.ranges ? want : p.ranges);
+  }
+  if (lane == 0) *out = SeqSpan{ps, pe, U, R};
+}
+
 template <int D>
 __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const DecodeParams p) {
-  grid_dependency_wait();  // records, prefix sums and (U, R) come from the decode kernel
   const int b = blockIdx.x;
-  const int64_t U = p.meta[0], R = p.meta[1];
-  const int64_t ps = p.prefix[b], pe = p.prefix[b + 1];
+  __shared__ SeqSpan span;
+  if (threadIdx.x < 32) combine_span(p, b, threadIdx.x, &span);
+  __syncthreads();
+  const int64_t U = span.U, R = span.R;
+  const int64_t ps = span.ps, pe = span.pe;
   if (pe <= ps) return;
   const int64_t f = range_of_page(ps, U, R), l = range_of_page(pe - 1, U, R);
-  if (f == l) return;
+  if (f == l) return;  // finished inside one range by the decode kernel
+  grid_dependency_wait();  // the records come from the decode kernel
   const int n = static_cast<int>(l - f + 1);
   const int64_t rec_first = f * 2 + (ps > range_start(f, U, R) ? 1 : 0);
   constexpr int kQuads = D / 4;
@@ -1980,6 +2115,7 @@ cudaError_t launch_decode(const Plan& pl, const CUtensorMap& km, const CUtensorM
   }
   // head blocks of one range are adjacent in launch order: they share the
   // page's scale sectors and DRAM rows
+  p.ranges = ranges;
   dim3 grid(p.hkv / pl.hb, ranges);
   pl.fn<<<grid, (pl.nw + 1) * 32, ls.smem, stream>>>(km, vm, p);
   e = cudaGetLastError();
@@ -2108,6 +2244,7 @@ static int decode_entry(bool fp16, const void* query, const void* k_data, const 
   p.hb = 0;
   p.qpk = qpk;
   p.stages = 0;
+  p.ranges = 0;
   p.out_mode = out_mode;
   p.scale_log2 = static_cast<float>(static_cast<double>(softmax_scale) * 1.4426950408889634);
 
