@@ -79,6 +79,7 @@ struct DecodeParams {
   int32_t stages;
   int32_t out_mode;
   int32_t ranges;            // page ranges launched (the decode grid's y extent)
+  int32_t combine_lanes;     // lanes of the combine merging one output quad (1, 2, 4 or 8)
   float scale_log2;          // softmax_scale * log2(e)
 };
 
@@ -1598,15 +1599,14 @@ __global__ void __maxnreg__(128) decode_fp16_kernel(const __grid_constant__ CUte
 }
 
 // ---------------------------------------------------------- combine kernel
-// kCombineSplit CTAs per sequence, each a share of its (query head, 4 dims)
-// items (more SMs take part than with one CTA per sequence): an item merges
-// the records of the ranges the sequence touches (record k: the first
-// range's record, then side 0 of each later range).  Records are read eight
-// at a time with an online rescale, so a typical sequence (a few ranges)
-// costs one round of loads.  Sequences finished inside one range were written
-// by the decode kernel and are skipped.
+// Grid (sequence, share): the CTAs of a sequence split its (query head,
+// 4 dims) items, so many SMs take part.  An item merges the records of the
+// ranges the sequence touches (record k: the first range's record, then
+// side 0 of each later range), eight per load round with an online rescale,
+// spread over combine_lanes adjacent lanes when a sequence spans many
+// ranges.  Sequences finished inside one range were written by the decode
+// kernel and are skipped.
 constexpr int kCombineThreads = 256;
-constexpr int kCombineSplit = 4;  // CTAs per sequence, each a quarter of its (query head, 4 dims) items
 
 // Where sequence b's pages sit in the batch's concatenation, the total U and
 // the ranges R in use, recomputed from seq_lens exactly as the decode's plan
@@ -1660,18 +1660,25 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const D
   const int n = static_cast<int>(l - f + 1);
   const int64_t rec_first = f * 2 + (ps > range_start(f, U, R) ? 1 : 0);
   constexpr int kQuads = D / 4;
-  const int items = p.hq * kQuads, per = (items + kCombineSplit - 1) / kCombineSplit;
-  const int i0 = blockIdx.y * per, i1 = min(items, i0 + per);
-  for (int item = i0 + threadIdx.x; item < i1; item += blockDim.x) {
-    const int qh = item / kQuads, t = item % kQuads;
-    float m = kNegInf, wsum = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k0 = 0; k0 < n; k0 += 8) {
+  // T adjacent lanes share one (query head, 4 dims) item: lane j of the group
+  // merges records j, j + T, j + 2T, ... (eight per load round), then the
+  // group combines its partial merges with shuffles.  Sequences split over
+  // many ranges (small batches) thus need one or two load rounds, not n / 8.
+  const int T = p.combine_lanes;
+  const int items = p.hq * kQuads;
+  const int slot = blockIdx.y * blockDim.x + threadIdx.x;
+  const int item = slot / T, j = slot % T;
+  const bool valid = item < items;
+  const int qh = item / kQuads, t = item % kQuads;
+  float m = kNegInf, wsum = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (valid) {
+    for (int k0 = j; k0 < n; k0 += 8 * T) {
       float lse[8];
       float4 o[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const int k = k0 + i;
+        const int k = k0 + i * T;
         if (k < n) {
           const int64_t rec = k == 0 ? rec_first : (f + k) * 2;
           lse[i] = p.rec_lse[rec * p.hq + qh];
@@ -1701,6 +1708,23 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const D
       }
       m = mc;
     }
+  }
+  // the group's lanes are adjacent (T divides 32): combine their partial merges
+  for (int o = 1; o < T; o <<= 1) {
+    const float mo = __shfl_xor_sync(0xffffffffu, m, o);
+    const float wo = __shfl_xor_sync(0xffffffffu, wsum, o);
+    const float ax = __shfl_xor_sync(0xffffffffu, acc.x, o), ay = __shfl_xor_sync(0xffffffffu, acc.y, o);
+    const float az = __shfl_xor_sync(0xffffffffu, acc.z, o), aw = __shfl_xor_sync(0xffffffffu, acc.w, o);
+    const float mn = fmaxf(m, mo);
+    const float cs = mn == kNegInf ? 0.f : ex2(m - mn), co = mn == kNegInf ? 0.f : ex2(mo - mn);
+    acc.x = acc.x * cs + ax * co;
+    acc.y = acc.y * cs + ay * co;
+    acc.z = acc.z * cs + az * co;
+    acc.w = acc.w * cs + aw * co;
+    wsum = wsum * cs + wo * co;
+    m = mn;
+  }
+  if (valid && j == 0) {
     const float inv = 1.0f / wsum;
     const int64_t orow = static_cast<int64_t>(b) * p.hq + qh;
     if (p.out_mode == IRIS_DECODE_OUT_FP16) {
@@ -2124,8 +2148,15 @@ cudaError_t launch_decode(const Plan& pl, const CUtensorMap& km, const CUtensorM
     return e;
   }
   // programmatic launch: the combine CTAs are resident before the decode ends
+  // lanes per output item: enough that each merges at most ~8 records in one
+  // load round (a sequence spans up to about ranges / batch + 2 ranges)
+  const int rec_est = ranges / p.batch + 2;
+  int lanes = 1;
+  while (lanes < 8 && (rec_est + lanes - 1) / lanes > 8) lanes <<= 1;
+  p.combine_lanes = lanes;
+  const int slots = p.hq * (D / 4) * lanes;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.batch, kCombineSplit);
+  cfg.gridDim = dim3(p.batch, (slots + kCombineThreads - 1) / kCombineThreads);
   cfg.blockDim = dim3(kCombineThreads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
@@ -2245,6 +2276,7 @@ static int decode_entry(bool fp16, const void* query, const void* k_data, const 
   p.qpk = qpk;
   p.stages = 0;
   p.ranges = 0;
+  p.combine_lanes = 1;
   p.out_mode = out_mode;
   p.scale_log2 = static_cast<float>(static_cast<double>(softmax_scale) * 1.4426950408889634);
 
