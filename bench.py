@@ -712,9 +712,10 @@ def c4_self_check(c4, dec4, out, dist, rank, world, dev):
 
 def c4_breakdown(c4, dec4, steps, dev, dist, warmup):
     """Per-stage device times of the split-context step, each stage replayed
-    from its own graph: the local LSE decode, the NCCL all-gather, the merge.
-    Returns max-over-ranks ms per step of each, and the min over ranks of the
-    decode (the spread is the rank skew the all-gather absorbs)."""
+    from its own graph: the local LSE decode (into the exchange buffer for
+    the NVLink transport), then the peer-memory merge, or for NCCL the
+    all-gather and the merge.  Returns max-over-ranks us per step of each, and the min over ranks
+    of the decode (the spread is the rank skew the exchange absorbs)."""
     from iris_kernel.fused_attention import decode_partial, merge_lse_packed
 
     plan = dec4.plan
@@ -730,8 +731,12 @@ def c4_breakdown(c4, dec4, steps, dev, dist, warmup):
         merge_lse_packed(dec4.recv if dist is not None else dec4.send, dec4.world, plan.batch, C4_HQ, D,
                          dec4.output)
 
+    stages = [("decode", dec)]
+    if dec4.xchg is not None:
+        stages += [("p2p_merge", lambda: dec4.xchg.merge(dec4.output.view(-1, D)))]
+    else:
+        stages += [("merge", merge)] + ([("allgather", gather)] if dist is not None else [])
     res = {}
-    stages = [("decode", dec), ("merge", merge)] + ([("allgather", gather)] if dist is not None else [])
     for name, fn in stages:
         g = graph_of(fn, dev)
         ms = timed(g.replay, steps, dev, dist, warmup) / steps
@@ -836,22 +841,33 @@ def main():
         from iris_kernel import parallel
 
         c4 = build_c4(dev, rank, world, seed=44 + rank)
-        dec4 = parallel.SplitContextDecoder(c4["plan"], c4["bt"], C4_HQ, D)
-        iris_kernel.set_validation_mode("deferred")
-        g_c4 = graph_of(lambda: dec4(c4["q"], c4["kd"], c4["vd"], c4["ks"], c4["vs"]), dev)
-        ms_c4 = timed(g_c4.replay, x_steps, dev, dist, args.warmup)
-        iris_kernel.check_errors(dev)
-        del g_c4  # the graph holds an NCCL call: released before the process group
-        c4_us = reduce_over_ranks(ms_c4, dist, dev) / x_steps * 1e3
-        parts = c4_breakdown(c4, dec4, x_steps, dev, dist, args.warmup)
-        iris_kernel.set_validation_mode("sync")
-        out4 = dec4(c4["q"], c4["kd"], c4["vd"], c4["ks"], c4["vs"])
-        torch.cuda.synchronize(dev)
-        check = c4_self_check(c4, dec4, out4, dist, rank, world, dev)
+        # over NVLink peer memory at N > 1 (CUDA IPC exchange buffers, one merge kernel reading every
+        # GPU's partial); NCCL all-gather + merge timed beside it
+        transports = ["p2p", "nccl"] if world > 1 else ["nccl"]
+        times = {}
+        for tr in transports:
+            dec4 = parallel.SplitContextDecoder(c4["plan"], c4["bt"], C4_HQ, D, transport=tr)
+            iris_kernel.set_validation_mode("deferred")
+            g_c4 = graph_of(lambda: dec4(c4["q"], c4["kd"], c4["vd"], c4["ks"], c4["vs"]), dev)
+            ms_c4 = timed(g_c4.replay, x_steps, dev, dist, args.warmup)
+            iris_kernel.check_errors(dev)
+            del g_c4  # a graph holding an NCCL call is released before the process group
+            times[tr] = reduce_over_ranks(ms_c4, dist, dev) / x_steps * 1e3
+            if tr == transports[0]:
+                parts = c4_breakdown(c4, dec4, x_steps, dev, dist, args.warmup)
+                iris_kernel.set_validation_mode("sync")
+                out4 = dec4(c4["q"], c4["kd"], c4["vd"], c4["ks"], c4["vs"])
+                torch.cuda.synchronize(dev)
+                check = c4_self_check(c4, dec4, out4, dist, rank, world, dev)
+            iris_kernel.set_validation_mode("sync")
+            dec4.close()
+            del dec4
+        c4_us = times[transports[0]]
         extra["c4"] = {"us": c4_us, "tbs": C4_BYTES / (c4_us * 1e-6) / 1e12,
-                       "frac": C4_BYTES / (c4_us * 1e-6) / 1e9 / (world * peak),
+                       "frac": C4_BYTES / (c4_us * 1e-6) / 1e9 / (world * peak), "transport": transports[0],
+                       **({"nccl_us": round(times["nccl"], 2)} if world > 1 else {}),
                        **{k: round(v, 2) for k, v in parts.items()}, "check": check}
-        del dec4, c4
+        del c4
     # ---- the matched FP16 decode on the config-2 shape ----
     if run("f16") and world == 1:
         from iris_kernel.fused_attention import fused_fp16_paged_decode_attention

@@ -19,7 +19,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 OUT = os.path.join(HERE, "iris_kernel", "libiris_b200.so")
-SOURCES = ["append.cu", "decode.cu", "decode_noalloc.cu"]
+SOURCES = ["append.cu", "decode.cu", "decode_noalloc.cu", "exchange.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -1,0 +1,277 @@
+// Split-context merge over NVLink peer memory (no collective library).
+//
+// In split-context decode every GPU computes, for the whole batch, a
+// log-sum-exp partial (O [rows, D] fp32 normalised, lse [rows] fp32) over the
+// context splits it holds, and every GPU needs the merge of all of them.
+// Instead of an all-gather followed by a merge, each GPU's decode writes its
+// partial straight into an exchange buffer that the other GPUs have mapped
+// (CUDA IPC), and one kernel per GPU and step reads every GPU's partial from
+// its owner's memory over NVLink and writes the merged fp16 output.  The data
+// crosses NVLink once, inside the kernel that consumes it, and a step is the
+// decode plus this one kernel.
+//
+// Exchange buffer of one GPU (cudaMalloc'ed, zeroed, mapped by the peers):
+//   header (256 B): [0]   flag    = the step whose partial the buffer holds
+//                                   (system-scope release by the owner)
+//                   [64]  epoch   = the owner's step counter
+//                   [128] readers = peers' reads of this buffer completed
+//                                   (system-scope adds by the peers)
+//                   [192] count   = CTA arrivals of the running merge
+//   then O [rows, D] fp32 and lse [rows] fp32.
+// Step e of the merge on one GPU: every CTA raises the GPU's flag to e (the
+// decode that wrote the partial ran before the merge in the stream), waits
+// until every GPU's flag reaches e, and merges its rows from all buffers; the
+// last CTA to finish adds one to every peer's `readers`, then waits until its
+// own `readers` reaches (GPUs - 1) * e, i.e. every peer has finished reading
+// this GPU's partial of step e, before the kernel ends.  So the next step's
+// decode, which follows the merge in the stream, never overwrites a partial a
+// peer may still read, and a peer never reads a partial before its flag says
+// it is complete.  Every GPU runs the merge once per step, in the same order.
+// Waits are bounded: a GPU that does not arrive within the limit makes the
+// merge set IRIS_ERR_PIPELINE_TIMEOUT (the exchange must then be rebuilt).
+// No multicast, no library kernel on peer memory.
+#include <cstring>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr int kMaxRanks = 8;
+constexpr int kXchgThreads = 256;
+
+struct Header {
+  unsigned long long flag;
+  unsigned long long pad0[7];
+  unsigned long long epoch;
+  unsigned long long pad1[7];
+  unsigned long long readers;
+  unsigned long long pad2[7];
+  unsigned int count;
+};
+static_assert(sizeof(Header) <= IRIS_XCHG_HEADER_BYTES, "exchange header");
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ void red_release_sys_add(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Spin until *p >= want, at most limit_ns after t0; false when it gave up.
+__device__ __forceinline__ bool wait_at_least(const unsigned long long* p, unsigned long long want, uint64_t t0,
+                                              uint64_t limit_ns) {
+  while (ld_acquire_sys(p) < want) {
+    if (iris::globaltimer_ns() - t0 > limit_ns) return false;
+    __nanosleep(64);
+  }
+  return true;
+}
+
+struct Peers {
+  uint8_t* buf[kMaxRanks];
+};
+
+// One warp per row, 4 dims per lane and step; NR (the number of GPUs, a
+// compile-time constant) lets every GPU's loads of a row issue together, so a
+// row costs one NVLink round trip for its lse values and one for its O
+// values.  A part with lse = -inf holds none of the row's tokens and is
+// skipped (its O may hold anything).
+template <int NR>
+__global__ void __launch_bounds__(kXchgThreads) xchg_merge_kernel(Peers peers, int32_t me, int64_t rows,
+                                                                  int32_t head_dim, __half* __restrict__ out,
+                                                                  int32_t* err, uint64_t limit_ns) {
+  __shared__ int ok;
+  Header* mine = reinterpret_cast<Header*>(peers.buf[me]);
+  const unsigned long long e = *reinterpret_cast<volatile unsigned long long*>(&mine->epoch) + 1;
+  const uint64_t t0 = iris::globaltimer_ns();
+  if (threadIdx.x == 0) st_release_sys(&mine->flag, e);  // this GPU's partial of step e is complete
+  if (threadIdx.x < 32) {  // lane k waits for GPU k's flag
+    int good = 1;
+    if (threadIdx.x < NR)
+      good = wait_at_least(&reinterpret_cast<const Header*>(peers.buf[threadIdx.x])->flag, e, t0, limit_ns);
+    const unsigned all = __ballot_sync(0xffffffffu, good);
+    if (threadIdx.x == 0) ok = all == 0xffffffffu;
+  }
+  __syncthreads();
+  if (!ok) {
+    if (threadIdx.x == 0) iris::set_error(err, IRIS_ERR_PIPELINE_TIMEOUT);
+    return;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warps = blockDim.x >> 5;
+  const int64_t n_o = rows * head_dim;
+  const float kNegInf = -__int_as_float(0x7f800000);
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * warps + warp; row < rows;
+       row += static_cast<int64_t>(gridDim.x) * warps) {
+    float lse[NR];
+#pragma unroll
+    for (int k = 0; k < NR; ++k)
+      lse[k] = __ldcv(reinterpret_cast<const float*>(peers.buf[k] + IRIS_XCHG_HEADER_BYTES) + n_o + row);
+    float mx = kNegInf;
+#pragma unroll
+    for (int k = 0; k < NR; ++k) mx = fmaxf(mx, lse[k]);
+    for (int d = 4 * lane; d < head_dim; d += 128) {
+      float4 v[NR];
+#pragma unroll
+      for (int k = 0; k < NR; ++k)
+        v[k] = __ldcv(reinterpret_cast<const float4*>(
+            reinterpret_cast<const float*>(peers.buf[k] + IRIS_XCHG_HEADER_BYTES) + row * head_dim + d));
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      float ws = 0.f;
+#pragma unroll
+      for (int k = 0; k < NR; ++k) {
+        const bool has = lse[k] != kNegInf;
+        const float w = has ? iris::ex2(lse[k] - mx) : 0.f;
+        const float4 x = has ? v[k] : make_float4(0.f, 0.f, 0.f, 0.f);
+        acc.x = fmaf(w, x.x, acc.x);
+        acc.y = fmaf(w, x.y, acc.y);
+        acc.z = fmaf(w, x.z, acc.z);
+        acc.w = fmaf(w, x.w, acc.w);
+        ws += w;
+      }
+      const float inv = 1.0f / ws;
+      uint2 u;
+      u.x = iris::h2_as_u32(__floats2half2_rn(acc.x * inv, acc.y * inv));
+      u.y = iris::h2_as_u32(__floats2half2_rn(acc.z * inv, acc.w * inv));
+      *reinterpret_cast<uint2*>(out + row * head_dim + d) = u;
+    }
+  }
+  // the last CTA tells every peer that its partial has been read, then waits
+  // until every peer has read this GPU's
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned int done = atomicAdd(&mine->count, 1u);
+    if (done == gridDim.x - 1) {
+      mine->count = 0;
+#pragma unroll
+      for (int k = 0; k < NR; ++k)
+        if (k != me) red_release_sys_add(&reinterpret_cast<Header*>(peers.buf[k])->readers, 1ull);
+      if (!wait_at_least(&mine->readers, static_cast<unsigned long long>(NR - 1) * e, t0, limit_ns))
+        iris::set_error(err, IRIS_ERR_PIPELINE_TIMEOUT);
+      mine->epoch = e;
+    }
+  }
+}
+
+}  // namespace
+
+extern "C" size_t iris_b200_xchg_buffer_bytes(int64_t rows, int32_t head_dim) {
+  if (rows <= 0 || head_dim <= 0 || head_dim % 4 != 0) return 0;
+  return IRIS_XCHG_HEADER_BYTES + static_cast<size_t>(rows) * (head_dim + 1) * sizeof(float);
+}
+
+extern "C" int iris_b200_xchg_alloc(size_t bytes, void** buf) {
+  if (buf == nullptr || bytes < static_cast<size_t>(IRIS_XCHG_HEADER_BYTES)) return IRIS_EINVAL;
+  iris::clear_stale_cuda_error();
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    iris::record_cuda_error(e, "exchange buffer allocation");
+    if (p != nullptr) cudaFree(p);
+    return IRIS_ECUDA;
+  }
+  *buf = p;
+  return IRIS_OK;
+}
+
+extern "C" int iris_b200_xchg_free(void* buf) {
+  if (buf == nullptr) return IRIS_OK;
+  const cudaError_t e = cudaFree(buf);
+  if (e != cudaSuccess) {
+    iris::record_cuda_error(e, "cudaFree(exchange buffer)");
+    return IRIS_ECUDA;
+  }
+  return IRIS_OK;
+}
+
+extern "C" int iris_b200_ipc_export(const void* buf, void* handle) {
+  if (buf == nullptr || handle == nullptr) return IRIS_EINVAL;
+  iris::clear_stale_cuda_error();
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(buf));
+  if (e != cudaSuccess) {
+    iris::record_cuda_error(e, "cudaIpcGetMemHandle");
+    return IRIS_ECUDA;
+  }
+  static_assert(sizeof(h) == IRIS_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  return IRIS_OK;
+}
+
+extern "C" int iris_b200_ipc_open(const void* handle, void** peer_buf) {
+  if (handle == nullptr || peer_buf == nullptr) return IRIS_EINVAL;
+  iris::clear_stale_cuda_error();
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    iris::record_cuda_error(e, "cudaIpcOpenMemHandle");
+    return IRIS_ECUDA;
+  }
+  *peer_buf = p;
+  return IRIS_OK;
+}
+
+extern "C" int iris_b200_ipc_close(void* peer_buf) {
+  if (peer_buf == nullptr) return IRIS_OK;
+  const cudaError_t e = cudaIpcCloseMemHandle(peer_buf);
+  if (e != cudaSuccess) {
+    iris::record_cuda_error(e, "cudaIpcCloseMemHandle");
+    return IRIS_ECUDA;
+  }
+  return IRIS_OK;
+}
+
+extern "C" int iris_b200_xchg_merge(void* const* bufs, int32_t num_ranks, int32_t my_rank, int64_t rows,
+                                    int32_t head_dim, void* output, int32_t* error_word, int64_t limit_ns,
+                                    void* stream) {
+  if (bufs == nullptr || output == nullptr || num_ranks <= 0 || num_ranks > kMaxRanks || my_rank < 0 ||
+      my_rank >= num_ranks || rows <= 0 || head_dim <= 0 || head_dim % 4 != 0 || head_dim > 512 || limit_ns <= 0)
+    return IRIS_EINVAL;
+  Peers peers = {};
+  for (int k = 0; k < num_ranks; ++k) {
+    if (bufs[k] == nullptr || reinterpret_cast<uintptr_t>(bufs[k]) % 256 != 0) return IRIS_EALIGN;
+    peers.buf[k] = static_cast<uint8_t*>(bufs[k]);
+  }
+  if (reinterpret_cast<uintptr_t>(output) % 8 != 0) return IRIS_EALIGN;
+  iris::clear_stale_cuda_error();
+  const int64_t need = (rows + kXchgThreads / 32 - 1) / (kXchgThreads / 32);
+  const int grid = static_cast<int>(need < 148 ? need : 148);
+  __half* out = static_cast<__half*>(output);
+  const uint64_t lim = static_cast<uint64_t>(limit_ns);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (num_ranks) {  // one instance per GPU count
+#define IRIS_XCHG_CASE(N)                                                                                          \
+  case N:                                                                                                          \
+    xchg_merge_kernel<N><<<grid, kXchgThreads, 0, st>>>(peers, my_rank, rows, head_dim, out, error_word, lim); \
+    break;
+    IRIS_XCHG_CASE(1)
+    IRIS_XCHG_CASE(2)
+    IRIS_XCHG_CASE(3)
+    IRIS_XCHG_CASE(4)
+    IRIS_XCHG_CASE(5)
+    IRIS_XCHG_CASE(6)
+    IRIS_XCHG_CASE(7)
+    IRIS_XCHG_CASE(8)
+#undef IRIS_XCHG_CASE
+    default:
+      return IRIS_EUNSUPPORTED;
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    iris::record_cuda_error(e, "xchg_merge_kernel launch");
+    return IRIS_ECUDA;
+  }
+  return IRIS_OK;
+}

@@ -66,7 +66,18 @@ SIGNATURES = {
         ctypes.c_int,
         [_c_p, _c_p, _c_p, _c_p, _c_i64, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i64, _c_i32,
          _c_i32, _c_f, _c_p, _c_sz, _c_p, _c_p]),
+    "iris_b200_xchg_buffer_bytes": (_c_sz, [_c_i64, _c_i32]),
+    "iris_b200_xchg_alloc": (ctypes.c_int, [_c_sz, ctypes.POINTER(_c_p)]),
+    "iris_b200_xchg_free": (ctypes.c_int, [_c_p]),
+    "iris_b200_ipc_export": (ctypes.c_int, [_c_p, _c_p]),
+    "iris_b200_ipc_open": (ctypes.c_int, [_c_p, ctypes.POINTER(_c_p)]),
+    "iris_b200_ipc_close": (ctypes.c_int, [_c_p]),
+    "iris_b200_xchg_merge": (ctypes.c_int, [ctypes.POINTER(_c_p), _c_i32, _c_i32, _c_i64, _c_i32, _c_p, _c_p, _c_i64,
+                                            _c_p]),
 }
+
+IPC_HANDLE_BYTES = 64  # IRIS_IPC_HANDLE_BYTES
+XCHG_HEADER_BYTES = 256  # IRIS_XCHG_HEADER_BYTES
 
 
 def _load() -> ctypes.CDLL:

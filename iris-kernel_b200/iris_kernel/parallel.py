@@ -21,15 +21,24 @@ spreads a decode batch over N GPUs of a node (torch.distributed, NCCL):
   in a partly filled page, which the concatenation keeps last.
 
 Nothing here moves KV pages between GPUs; remote data arrives only as the
-gathered partials, through NCCL.
+partials.  Two transports carry them:
+
+* ``"nccl"``: one ``all_gather_into_tensor`` of the packed partials, then
+  the merge kernel;
+* ``"p2p"`` (:class:`PeerExchange`): each GPU's decode writes its partial
+  straight into a buffer the other GPUs have mapped (CUDA IPC), and one merge
+  kernel per GPU reads every partial from its owner's memory over NVLink,
+  with bounded waits on per-GPU step flags (``iris_b200_xchg_*``).
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import numpy as np
 import torch
 
+from . import _lib, _runtime
 from .fused_attention import decode_partial, merge_lse_packed
 
 
@@ -155,17 +164,115 @@ def pack_partials(o_local: torch.Tensor, lse_local: torch.Tensor, seqs, batch: i
     return buf
 
 
+def _device_floats(ptr: int, n: int, device: torch.device) -> torch.Tensor:
+    """A float32 tensor of ``n`` elements over device memory the library
+    allocated (no copy; the caller keeps the memory alive)."""
+
+    class _Mem:
+        __cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3,
+                                    "strides": None}
+
+    with torch.cuda.device(device):
+        return torch.as_tensor(_Mem(), device=device)
+
+
+class PeerExchange:
+    """Split-context merge over NVLink peer memory for one GPU of a process
+    group: an exchange buffer on this GPU, mapped by every other GPU of the
+    group (CUDA IPC handles swapped over the group once), and the mapped
+    addresses of theirs.  Per step every GPU writes its LSE-form partial into
+    :attr:`o` ``[rows, D]`` and :attr:`lse` ``[rows]`` (fp32 tensors over its
+    own buffer; the decode writes them directly), then calls :meth:`merge`;
+    both are CUDA-graph capturable.  A GPU that does not arrive within
+    ``limit_s`` makes the merge record a pipeline timeout (raised as
+    RuntimeError) instead of waiting forever; the exchange must then be
+    rebuilt.  Call :meth:`close` on every GPU (it synchronises the group)
+    before destroying the process group."""
+
+    def __init__(self, rows: int, head_dim: int, *, group=None, limit_s: float = 2.0):
+        import torch.distributed as dist
+
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.rows, self.head_dim = rows, head_dim
+        self.limit_ns = int(limit_s * 1e9)
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        lib = _lib.lib
+        nbytes = lib.iris_b200_xchg_buffer_bytes(rows, head_dim)
+        if nbytes == 0:
+            raise ValueError("exchange buffer: rows > 0 and head_dim a multiple of 4 required")
+        buf = ctypes.c_void_p()
+        _lib.check_status(lib.iris_b200_xchg_alloc(nbytes, ctypes.byref(buf)), "iris_b200_xchg_alloc")
+        self.buf = buf.value
+        self.partial = _device_floats(self.buf + _lib.XCHG_HEADER_BYTES, rows * (head_dim + 1), self.device)
+        self.o = self.partial[:rows * head_dim].view(rows, head_dim)
+        self.lse = self.partial[rows * head_dim:]
+        self.peers: list[int] = []
+        ptrs = []
+        if self.world > 1:
+            handle = (ctypes.c_char * _lib.IPC_HANDLE_BYTES)()
+            _lib.check_status(lib.iris_b200_ipc_export(self.buf, ctypes.addressof(handle)), "iris_b200_ipc_export")
+            handles: list = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            for k, h in enumerate(handles):
+                if k == self.rank:
+                    ptrs.append(self.buf)
+                    continue
+                hb = (ctypes.c_char * _lib.IPC_HANDLE_BYTES).from_buffer_copy(h)
+                p = ctypes.c_void_p()
+                _lib.check_status(lib.iris_b200_ipc_open(ctypes.addressof(hb), ctypes.byref(p)), "iris_b200_ipc_open")
+                self.peers.append(p.value)
+                ptrs.append(p.value)
+        else:
+            ptrs.append(self.buf)
+        self.bufs = (ctypes.c_void_p * self.world)(*ptrs)
+
+    def merge(self, output: torch.Tensor) -> torch.Tensor:
+        """Merge every GPU's partial of this step into ``output [rows, D]``
+        fp16 (this GPU's partial must be in :attr:`o` / :attr:`lse`, written
+        earlier on the current stream)."""
+        word = _runtime.error_word(self.device)
+        _lib.check_status(
+            _lib.lib.iris_b200_xchg_merge(self.bufs, self.world, self.rank, self.rows, self.head_dim,
+                                          output.data_ptr(), word.data_ptr(), self.limit_ns,
+                                          _runtime.stream_ptr(self.device)),
+            "iris_b200_xchg_merge")
+        if _runtime.validation_mode() == "sync":
+            _runtime.raise_for_bits(_runtime.read_and_clear(word))
+        return output
+
+    def close(self) -> None:
+        import torch.distributed as dist
+
+        if self.buf is None:
+            return
+        torch.cuda.synchronize(self.device)
+        self.partial = self.o = self.lse = None  # views of the buffer freed below
+        for p in self.peers:
+            _lib.lib.iris_b200_ipc_close(p)
+        self.peers = []
+        if self.world > 1:
+            dist.barrier(group=self.group)  # no GPU still maps this buffer
+        _lib.lib.iris_b200_xchg_free(self.buf)
+        self.buf = None
+
+
 class SplitContextDecoder:
     """Split-context decode for one GPU's plan, with everything that does not
     change between steps (the local block table, the token counts, the
-    all-gather buffers) prepared once, so a step is three kernels and one
-    all-gather that a CUDA graph can capture.
+    exchange buffers) prepared once, so that a CUDA graph can capture a step.
+    With ``transport="nccl"`` a step is the LSE decode, one all-gather and
+    the merge kernel; with ``"p2p"`` the decode writes into the
+    :class:`PeerExchange` buffer and one merge kernel reads the other GPUs'
+    partials over NVLink (call :meth:`close` on every GPU before the process
+    group goes).
 
     ``block_table`` maps this GPU's splits to pages of its own cache; entries
     of other GPUs' splits are not read."""
 
     def __init__(self, plan: SplitPlan, block_table: torch.Tensor, num_q_heads: int, head_dim: int, *, group=None,
-                 page_size: int = 16, group_size: int = 32, softmax_scale=None):
+                 page_size: int = 16, group_size: int = 32, softmax_scale=None, transport: str = "nccl"):
         import torch.distributed as dist
 
         self.plan, self.group = plan, group
@@ -178,16 +285,33 @@ class SplitContextDecoder:
         self.local_bt = local_block_table(plan, block_table)
         self.lens = torch.from_numpy(plan.lens.astype(np.int32)).to(dev)
         self.idx = torch.from_numpy(plan.seqs).to(dev)
+        if transport not in ("nccl", "p2p"):
+            raise ValueError("transport must be 'nccl' or 'p2p'")
+        self.transport = transport
         n = packed_size(plan.batch, num_q_heads, head_dim)
-        self.send = torch.zeros(n, dtype=torch.float32, device=dev)
-        self.recv = torch.empty(self.world * n, dtype=torch.float32, device=dev)
+        if transport == "p2p":
+            # the exchange buffer's partial has the packed layout: the decode writes it directly
+            self.xchg = PeerExchange(plan.batch * num_q_heads, head_dim, group=group)
+            self.send, self.recv = self.xchg.partial, None
+        else:
+            self.xchg = None
+            self.send = torch.zeros(n, dtype=torch.float32, device=dev)
+            self.recv = torch.empty(self.world * n, dtype=torch.float32, device=dev)
         self.output = torch.empty((plan.batch, num_q_heads, head_dim), dtype=torch.float16, device=dev)
         o, lse = packed_views(self.send, plan.batch, num_q_heads, head_dim)
+        o.zero_()
         lse.fill_(float("-inf"))  # sequences without local tokens keep lse = -inf
         self._o, self._lse = o, lse
         m = len(plan.seqs)
         self._o_l = torch.empty((m, num_q_heads, head_dim), dtype=torch.float32, device=dev)
         self._lse_l = torch.empty((m, num_q_heads), dtype=torch.float32, device=dev)
+
+    def close(self) -> None:
+        """Release the peer exchange (every GPU of the group must call it)."""
+        if self.xchg is not None:
+            self.send = self._o = self._lse = None  # views of the exchange buffer
+            self.xchg.close()
+            self.xchg = None
 
     def __call__(self, query, k_data, v_data, k_scale, v_scale) -> torch.Tensor:
         import torch.distributed as dist
@@ -204,6 +328,9 @@ class SplitContextDecoder:
                                self.lens, out=self._o_l, lse=self._lse_l, **self.kw)
                 self._o.index_copy_(0, self.idx, self._o_l)
                 self._lse.index_copy_(0, self.idx, self._lse_l)
+        if self.xchg is not None:
+            self.xchg.merge(self.output.view(-1, self.d))
+            return self.output
         if self.world > 1:
             dist.all_gather_into_tensor(self.recv, self.send, group=self.group)
             parts = self.recv

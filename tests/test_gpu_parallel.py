@@ -7,9 +7,10 @@
   split assignments.
 * The packed merge ignores parts whose lse is -inf (their O may be garbage).
 * Sequence sharding: per-shard decodes reassembled equal the oracle.
-* With two or more GPUs: split-context over NCCL between two processes, each
-  GPU's cache holding only its own splits' pages (every other page poisoned
-  with NaN scales), equals the oracle on both ranks."""
+* With two or more GPUs: split-context between two processes, each GPU's
+  cache holding only its own splits' pages (every other page poisoned with
+  NaN scales), over NCCL and over NVLink peer memory (eager and replayed
+  from a CUDA graph), equals the oracle on both ranks."""
 import datetime
 import os
 import socket
@@ -167,6 +168,36 @@ def _nccl_worker(rank, world, port, c, expected):
         out2 = dec(t["query"], t["k_data"], t["v_data"], t["k_scale"], t["v_scale"])
         torch.cuda.synchronize()
         assert torch.equal(out2, out)
+        # the same over NVLink peer memory (CUDA IPC exchange buffers, no NCCL in the step):
+        # eager calls, then a CUDA graph replayed twice (each step's merge waits for the
+        # other GPU's partial, and for its read of this GPU's, before the next decode)
+        p2p = P.SplitContextDecoder(plan, t["block_table"], t["query"].shape[1], t["query"].shape[2],
+                                    transport="p2p")
+        try:
+            out3 = p2p(t["query"], t["k_data"], t["v_data"], t["k_scale"], t["v_scale"]).clone()
+            torch.cuda.synchronize()
+            assert_decode_close(out3, expected)
+            import iris_kernel
+
+            iris_kernel.set_validation_mode("deferred")
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                p2p(t["query"], t["k_data"], t["v_data"], t["k_scale"], t["v_scale"])
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                out4 = p2p(t["query"], t["k_data"], t["v_data"], t["k_scale"], t["v_scale"])
+            for _ in range(2):
+                out4.zero_()
+                g.replay()
+                torch.cuda.synchronize()
+                iris_kernel.check_errors()
+                assert_decode_close(out4, expected)
+            iris_kernel.set_validation_mode("sync")
+            del g
+        finally:
+            p2p.close()
     finally:
         dist.destroy_process_group()
 
