@@ -9,7 +9,9 @@ by a random permutation; K/V ~N(0,1) fp16 with 4 outlier K channels x8,
 written by the fused append), then per step
 
     decode attention over the 4096 cached tokens of every sequence, and
-    a batched 1-token fused RoPE+INT4 append per sequence at position 4096.
+    a batched 1-token fused RoPE+INT4 append per sequence at position 4096
+    (the next step's token; the decode does not read it, so the step's graph
+    runs the append beside the decode rather than after it).
 
 One process per GPU (torchrun for N > 1).  The 64 sequences are sharded
 64/N per GPU (sequence sharding: no collective), so the total work is fixed
@@ -26,8 +28,8 @@ deferred mode, no host syncs).  Inputs (303 MB per step at N=1) exceed the
 per step the new query / K / V / positions / slots are copied from pinned
 host memory, the decode and append calls run, the fp16 output is copied
 back and the step's error word is read on the host.  The query copy comes
-first and the decode starts as soon as it lands; the K/V copy runs on a
-second stream meanwhile, and the output copy overlaps the append.
+first and the decode starts as soon as it lands; the K/V copy and the
+append run on a second stream meanwhile.
 
 Also reported: config 5b prefill append, config 5a decode-style append,
 config 4 split-context decode over the ranks (one NCCL all-gather per step,
@@ -794,8 +796,20 @@ def main():
             fused_rope_int4_paged_append(w["knew"], w["vnew"], w["newpos"], w["newslot"], w["cos"], w["sin"],
                                          w["kd"], w["vd"], w["ks"], w["vs"], rotary_dim=D, page_size=P)
 
+        side = torch.cuda.Stream(dev)
+
+        def step_both():
+            # the append writes token 4096 (page 256 of every sequence), which the decode over
+            # tokens 0..4095 does not read: the graph runs it as a second branch beside the decode
+            # (its 64-thread CTAs fit in the registers the decode leaves free on every SM)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                step_append()
+            step_decode()
+            torch.cuda.current_stream(dev).wait_stream(side)
+
         iris_kernel.set_validation_mode("deferred")
-        g_step = graph_of(lambda: (step_decode(), step_append()), dev)
+        g_step = graph_of(step_both, dev)
         g_dec = graph_of(step_decode, dev)
         g_app = graph_of(step_append, dev)
         clk = Clocks(local).__enter__()
@@ -963,9 +977,9 @@ def _round(d):
 def run_e2e(w, args, dev, dist, world):
     """The step through the public Python API with host buffers (deferred
     validation, the step's error word read on the host once per step).  The
-    query copy leads; the decode starts as soon as it has landed, the new
-    K/V copy runs meanwhile on a second stream, the append waits for it, and
-    the output copy overlaps the append.  Returns the line's e2e object."""
+    query copy leads and the decode starts as soon as it has landed, the
+    output copy right after it; the new K/V copy and the append run
+    meanwhile on a second stream.  Returns the line's e2e object."""
     import iris_kernel
     from iris_kernel.fused_attention import fused_int4_paged_decode_attention
     from iris_kernel.fused_kv import fused_rope_int4_paged_append
@@ -992,7 +1006,6 @@ def run_e2e(w, args, dev, dist, world):
     out_dev = torch.empty_like(w["out"])
     main = torch.cuda.current_stream(dev)
     side = torch.cuda.Stream(dev)
-    kv_ready, out_ready = torch.cuda.Event(), torch.cuda.Event()
     calls = {"dec": lambda: fused_int4_paged_decode_attention(q, w["kd"], w["vd"], w["ks"], w["vs"], w["bt"],
                                                               w["lens"], out_dev),
              "app": lambda: fused_rope_int4_paged_append(k, v, pp, ss, w["cos"], w["sin"], w["kd"], w["vd"], w["ks"],
@@ -1000,17 +1013,12 @@ def run_e2e(w, args, dev, dist, world):
 
     def e2e_step():
         dev_in[:q_bytes].copy_(host_in[:q_bytes], non_blocking=True)
-        with torch.cuda.stream(side):
-            side.wait_stream(main)
-            dev_in[q_bytes:].copy_(host_in[q_bytes:], non_blocking=True)
-            kv_ready.record(side)
+        side.wait_stream(main)  # the K/V copy follows the query copy
         calls["dec"]()
-        out_ready.record(main)
-        main.wait_event(kv_ready)
-        calls["app"]()
-        with torch.cuda.stream(side):
-            side.wait_event(out_ready)
-            hout.copy_(out_dev, non_blocking=True)
+        hout.copy_(out_dev, non_blocking=True)
+        with torch.cuda.stream(side):  # the append runs beside the decode (it writes token 4096 only)
+            dev_in[q_bytes:].copy_(host_in[q_bytes:], non_blocking=True)
+            calls["app"]()
         main.wait_stream(side)
         iris_kernel.check_errors(dev)  # one host read of the error word per step (syncs)
 

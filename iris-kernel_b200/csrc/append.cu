@@ -14,7 +14,9 @@
 // (token, kv-head) row, for both K and V (D/32 threads per row), so the group
 // absmax and scale need no communication and the 16 packed bytes leave in
 // one vector store.  The kernel is HBM-bound: per (token, head) it moves 4D
-// bytes in and D + D/8 bytes out.
+// bytes in and D + D/8 bytes out.  Small batches (decode steps) use a
+// latency-shaped form instead: one thread per half group, two adjacent lanes
+// sharing the absmax, in CTAs small enough to run beside a decode kernel.
 #include <cstdlib>
 #include <map>
 #include <mutex>
@@ -261,11 +263,7 @@ IRIS_DEV bool inline_batch_check(const int32_t* __restrict__ slots, const int32_
 // loads the lanes' 64-byte stride fetches each sector twice and the L1
 // throughput bounds the kernel).  Needs 32-byte aligned key / value / cos /
 // sin bases.
-//
-// kInline: the batch is small (at most kInlineCheckTokens tokens) and every
-// CTA validates all of it before storing, instead of a check kernel before
-// the launch.
-template <int D, bool kWide, bool kInline>
+template <int D, bool kWide>
 __global__ void __launch_bounds__(AppendCfg<D>::kThreads) rope_int4_append_kernel(const AppendParams p) {
   using C = AppendCfg<D>;
   const int tid = threadIdx.x;
@@ -298,16 +296,6 @@ __global__ void __launch_bounds__(AppendCfg<D>::kThreads) rope_int4_append_kerne
     }
   };
   constexpr int kStep = kWide ? 2 : 1;  // 16-byte vectors per load
-  if constexpr (kInline) {
-    // issued before the batch check, whose latency they then overlap
-#pragma unroll
-    for (int i = 0; i < 4; i += kStep) load_kv(i);
-  }
-
-  bool batch_bad = false;
-  if constexpr (kInline)  // while the loads above are in flight
-    batch_bad = inline_batch_check<C::kThreads>(p.slots, p.positions, static_cast<int>(p.num_tokens), p.num_slots,
-                                                p.max_position, p.err);
   if (tid == 0 && p.prefetch_rows > 0) {
     // the K / V rows of the CTA about one resident wave later go to L2 now,
     // so DRAM keeps streaming while this wave computes
@@ -333,7 +321,7 @@ __global__ void __launch_bounds__(AppendCfg<D>::kThreads) rope_int4_append_kerne
   const __half* srow = p.sin_cache + static_cast<size_t>(pos) * (D / 2) + 32 * pair;
 #pragma unroll
   for (int i = 0; i < 4; i += kStep) {
-    if constexpr (!kInline) load_kv(i);
+    load_kv(i);
     if constexpr (kWide) {
       ldg_nc_v8(crow + 8 * i, cs[i], cs[i + 1]);
       ldg_nc_v8(srow + 8 * i, sn[i], sn[i + 1]);
@@ -372,7 +360,7 @@ __global__ void __launch_bounds__(AppendCfg<D>::kThreads) rope_int4_append_kerne
   // means the batch is rejected: nothing is written, as the reference raises
   // before it writes.
   grid_dependency_wait();
-  if (batch_bad || (p.err != nullptr && (*p.err & kRejectBits) != 0)) return;
+  if (p.err != nullptr && (*p.err & kRejectBits) != 0) return;
   const uint32_t page = p.page_div.div(static_cast<uint32_t>(slot));
   const uint32_t off = static_cast<uint32_t>(slot) - page * static_cast<uint32_t>(p.page_size);
   const size_t crow_idx = (static_cast<size_t>(page) * p.page_size + off) * p.num_heads + h;  // cache row
@@ -380,6 +368,136 @@ __global__ void __launch_bounds__(AppendCfg<D>::kThreads) rope_int4_append_kerne
   *reinterpret_cast<uint4*>(p.v_data + crow_idx * (D / 2) + 16 * c) = vw;
   p.k_scale[crow_idx * (D / 32) + c] = ks;
   p.v_scale[crow_idx * (D / 32) + c] = vs;
+}
+
+// A small batch (at most kInlineCheckTokens tokens): one thread per half
+// quantisation group (16 dims), so a thread holds half the loads of the
+// kernel above in flight, and 64-thread CTAs of at most 64 registers a thread
+// (4096 registers, what a decode kernel at 3 CTAs of 160 threads x 128
+// registers leaves free on an SM: the append of a decode step runs on the
+// SMs beside the decode).  Every CTA validates the whole batch before storing
+// (no check kernel before the launch); the K / V loads are issued first and
+// overlap that check.  A group's two halves are adjacent lanes and share
+// their absmax with one shuffle, so the scale and the packed bytes are those
+// of the one-thread-per-group kernel.
+template <int D>
+struct SmallAppendCfg {
+  static constexpr int kTpr = D / 16;         // threads per row: half groups
+  static constexpr int kHalf = kTpr / 2;      // partner distance (D/2 dims) in half groups
+  static constexpr int kRows = 64 / kTpr;     // rows per CTA
+  static constexpr int kThreads = kRows * kTpr;
+};
+
+template <int D, bool kWide>
+__global__ void __launch_bounds__(SmallAppendCfg<D>::kThreads, 16) rope_int4_append_small_kernel(const AppendParams p) {
+  using C = SmallAppendCfg<D>;
+  const int tid = threadIdx.x;
+  const int c = tid % C::kTpr;  // half group within the row
+  const int g = c >> 1, hf = c & 1;
+  const uint32_t row = blockIdx.x * C::kRows + tid / C::kTpr;
+  const uint32_t nrows = static_cast<uint32_t>(p.num_tokens) * static_cast<uint32_t>(p.num_heads);
+  const bool in_range = row < nrows;
+  const uint32_t rr = in_range ? row : 0u;  // rows past the end read row 0 and store nothing
+  const uint32_t tok = p.heads_div.div(rr);
+  const uint32_t h = rr - tok * static_cast<uint32_t>(p.num_heads);
+  const int32_t slot = __ldg(p.slots + tok);
+  const int32_t pos = __ldg(p.positions + tok);
+
+  const bool lo_half = c < C::kHalf;
+  const int pair = lo_half ? c : c - C::kHalf;  // half group index into cos/sin
+  const int partner = lo_half ? c + C::kHalf : c - C::kHalf;
+  const __half* krow = p.key + static_cast<size_t>(rr) * D;
+  const __half* vrow = p.value + static_cast<size_t>(rr) * D;
+  uint4 ko[2], kp[2], vo[2], cs[2], sn[2];
+  if constexpr (kWide) {
+    ldg_nc_v8(krow + 16 * c, ko[0], ko[1]);
+    ldg_nc_v8(krow + 16 * partner, kp[0], kp[1]);
+    ldg_nc_v8(vrow + 16 * c, vo[0], vo[1]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      ko[i] = ldg_nc_v4(krow + 16 * c + 8 * i);
+      kp[i] = ldg_nc_v4(krow + 16 * partner + 8 * i);
+      vo[i] = ldg_nc_v4(vrow + 16 * c + 8 * i);
+    }
+  }
+  const bool batch_bad = inline_batch_check<C::kThreads>(p.slots, p.positions, static_cast<int>(p.num_tokens),
+                                                         p.num_slots, p.max_position, p.err);
+  // from here on a row's threads leave together (the pair shuffle below needs both halves)
+  if (batch_bad || !in_range || slot < 0) return;
+  {
+    int32_t bits = 0;
+    if (static_cast<int64_t>(slot) >= p.num_slots) bits |= IRIS_ERR_SLOT_RANGE;
+    if (pos < 0) bits |= IRIS_ERR_POS_NEGATIVE;
+    else if (static_cast<int64_t>(pos) >= p.max_position) bits |= IRIS_ERR_POS_RANGE;
+    if (bits) return;  // recorded by the batch check; never touch memory outside the tables
+  }
+  const __half* crow = p.cos_cache + static_cast<size_t>(pos) * (D / 2) + 16 * pair;
+  const __half* srow = p.sin_cache + static_cast<size_t>(pos) * (D / 2) + 16 * pair;
+  if constexpr (kWide) {
+    ldg_nc_v8(crow, cs[0], cs[1]);
+    ldg_nc_v8(srow, sn[0], sn[1]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      cs[i] = ldg_nc_v4(crow + 8 * i);
+      sn[i] = ldg_nc_v4(srow + 8 * i);
+    }
+  }
+
+  // RoPE with fp16 rounding after each op, as in the kernel above
+  uint4 kr[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const __half2* own = reinterpret_cast<const __half2*>(&ko[i]);
+    const __half2* par = reinterpret_cast<const __half2*>(&kp[i]);
+    const __half2* cc = reinterpret_cast<const __half2*>(&cs[i]);
+    const __half2* ss = reinterpret_cast<const __half2*>(&sn[i]);
+    __half2* out = reinterpret_cast<__half2*>(&kr[i]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __half2 pj = lo_half ? __hneg2(par[j]) : par[j];
+      out[j] = __hadd2(__hmul2_rn(own[j], cc[j]), __hmul2_rn(pj, ss[j]));
+    }
+  }
+
+  // the group's absmax over both halves (the max is exact and order-free)
+  const unsigned pair_mask = 3u << ((threadIdx.x & 31) & ~1);
+  const auto group_absmax = [&](const uint4 (&v)[2]) {
+    const __half2 m = __hmax2_nan(habs_max_vec(v[0]), habs_max_vec(v[1]));
+    const __half mine = __hmax_nan(__low2half(m), __high2half(m));
+    const unsigned short other = __shfl_xor_sync(pair_mask, __half_as_ushort(mine), 1);
+    return __hmax_nan(mine, __ushort_as_half(other));
+  };
+  const auto quant_half = [&](const uint4 (&v)[2], __half& scale16, uint2& packed) {
+    scale16 = group_scale(group_absmax(v));
+    const float sc = __half2float(scale16);
+    if (fabsf(sc) <= 3.0e38f) {
+      const float r = rcp_approx(sc);
+      packed.x = quant_pack_vec(v[0], sc, r);
+      packed.y = quant_pack_vec(v[1], sc, r);
+    } else {
+      const __half2* x = reinterpret_cast<const __half2*>(v);
+      const __half2 x0[4] = {x[0], x[1], x[2], x[3]}, x1[4] = {x[4], x[5], x[6], x[7]};
+      packed.x = quant_pack8_ieee(x0, sc);
+      packed.y = quant_pack8_ieee(x1, sc);
+    }
+  };
+  __half ks, vs;
+  uint2 kw, vw;
+  quant_half(kr, ks, kw);
+  quant_half(vo, vs, vw);
+  // an earlier rejected batch whose error is still pending refuses this one too
+  if (p.err != nullptr && (*p.err & kRejectBits) != 0) return;
+  const uint32_t page = p.page_div.div(static_cast<uint32_t>(slot));
+  const uint32_t off = static_cast<uint32_t>(slot) - page * static_cast<uint32_t>(p.page_size);
+  const size_t crow_idx = (static_cast<size_t>(page) * p.page_size + off) * p.num_heads + h;  // cache row
+  *reinterpret_cast<uint2*>(p.k_data + crow_idx * (D / 2) + 16 * g + 8 * hf) = kw;
+  *reinterpret_cast<uint2*>(p.v_data + crow_idx * (D / 2) + 16 * g + 8 * hf) = vw;
+  if (hf == 0) {
+    p.k_scale[crow_idx * (D / 32) + g] = ks;
+    p.v_scale[crow_idx * (D / 32) + g] = vs;
+  }
 }
 
 // One thread per token: range checks and duplicate detection through a
@@ -560,28 +678,31 @@ static cudaError_t resident_ctas(const void* fn, int threads, int smem, int64_t*
 
 template <int D>
 static cudaError_t launch_append(const AppendParams& p, cudaStream_t stream) {
-  using C = AppendCfg<D>;
   const int64_t rows = p.num_tokens * p.num_heads;
+  if (rows == 0) return cudaSuccess;
+  const auto aligned32 = [](const void* a) { return (reinterpret_cast<uintptr_t>(a) & 31) == 0; };
+  const bool wide = aligned32(p.key) && aligned32(p.value) && aligned32(p.cos_cache) && aligned32(p.sin_cache) &&
+                    append_wide_enabled();
+  AppendParams q = p;
+  q.prefetch_rows = 0;
+  if (p.num_tokens <= kInlineCheckTokens) {  // a small batch checks itself; an ordinary launch
+    using S = SmallAppendCfg<D>;
+    const auto fn = wide ? rope_int4_append_small_kernel<D, true> : rope_int4_append_small_kernel<D, false>;
+    fn<<<static_cast<unsigned>((rows + S::kRows - 1) / S::kRows), S::kThreads, 0, stream>>>(q);
+    return cudaGetLastError();
+  }
+  using C = AppendCfg<D>;
   const int64_t blocks = (rows + C::kRows - 1) / C::kRows;
-  if (blocks == 0) return cudaSuccess;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
-  // programmatic launch: starts while the check kernel before it finishes;
-  // a small batch checks itself and starts after its predecessor as usual
+  // programmatic launch: starts while the check kernel before it finishes
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.stream = stream;
   cfg.attrs = attr;
-  cfg.numAttrs = p.num_tokens <= kInlineCheckTokens ? 0 : 1;
-  const auto aligned32 = [](const void* a) { return (reinterpret_cast<uintptr_t>(a) & 31) == 0; };
-  const bool wide = aligned32(p.key) && aligned32(p.value) && aligned32(p.cos_cache) && aligned32(p.sin_cache) &&
-                    append_wide_enabled();
-  const bool small = p.num_tokens <= kInlineCheckTokens;
-  const auto fn = small ? (wide ? rope_int4_append_kernel<D, true, true> : rope_int4_append_kernel<D, false, true>)
-                        : (wide ? rope_int4_append_kernel<D, true, false> : rope_int4_append_kernel<D, false, false>);
-  AppendParams q = p;
-  q.prefetch_rows = 0;
+  cfg.numAttrs = 1;
+  const auto fn = wide ? rope_int4_append_kernel<D, true> : rope_int4_append_kernel<D, false>;
   const int quarters = append_prefetch_quarters();
   if (quarters > 0) {
     int64_t resident = 0;

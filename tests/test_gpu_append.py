@@ -132,12 +132,14 @@ def test_large_batches_all_rows_bit_exact(H, D):
     _assert_bytes_equal(_fused(c), _oracle(c))
 
 
-def test_sixteen_byte_aligned_inputs_take_the_narrow_loads():
+@pytest.mark.parametrize("T,D", [(300, 128), (100, 128), (37, 64)])
+def test_sixteen_byte_aligned_inputs_take_the_narrow_loads(T, D):
     """K / V / cos / sin bases that are 16- but not 32-byte aligned use the
-    16-byte load form; the result is the same bytes."""
+    16-byte load form of either kernel (large batches, and batches of at most
+    128 tokens); the result is the same bytes."""
     from iris_kernel.fused_kv import fused_rope_int4_paged_append
 
-    c = cases.append_outliers(seed=5, T=300, H=8, D=128, P=16, NP=32, max_pos=512)
+    c = cases.append_outliers(seed=5 + T, T=T, H=8, D=D, P=16, NP=32, max_pos=512)
     ref = _oracle(c)
     t = to_dev(c, cases.APPEND_KEYS)
 
