@@ -979,7 +979,10 @@ def run_e2e(w, args, dev, dist, world):
     validation, the step's error word read on the host once per step).  The
     query copy leads and the decode starts as soon as it has landed, the
     output copy right after it; the new K/V copy and the append run
-    meanwhile on a second stream.  Returns the line's e2e object."""
+    meanwhile on a second stream.  ``graph_ms_per_step``: the same step,
+    copies included, captured once in a CUDA graph and replayed (one
+    launch per step), with the same host read.  Returns the line's e2e
+    object."""
     import iris_kernel
     from iris_kernel.fused_attention import fused_int4_paged_decode_attention
     from iris_kernel.fused_kv import fused_rope_int4_paged_append
@@ -1004,33 +1007,38 @@ def run_e2e(w, args, dev, dist, world):
     q, k, v, pp, ss = (view(dev_in, name, t) for name, t in parts)
     q_bytes = offs["k"]
     out_dev = torch.empty_like(w["out"])
-    main = torch.cuda.current_stream(dev)
     side = torch.cuda.Stream(dev)
     calls = {"dec": lambda: fused_int4_paged_decode_attention(q, w["kd"], w["vd"], w["ks"], w["vs"], w["bt"],
                                                               w["lens"], out_dev),
              "app": lambda: fused_rope_int4_paged_append(k, v, pp, ss, w["cos"], w["sin"], w["kd"], w["vd"], w["ks"],
                                                          w["vs"], rotary_dim=D, page_size=P)}
 
-    def e2e_step():
+    def body():
+        cur = torch.cuda.current_stream(dev)
         dev_in[:q_bytes].copy_(host_in[:q_bytes], non_blocking=True)
-        side.wait_stream(main)  # the K/V copy follows the query copy
+        side.wait_stream(cur)  # the K/V copy follows the query copy
         calls["dec"]()
         hout.copy_(out_dev, non_blocking=True)
         with torch.cuda.stream(side):  # the append runs beside the decode (it writes token 4096 only)
             dev_in[q_bytes:].copy_(host_in[q_bytes:], non_blocking=True)
             calls["app"]()
-        main.wait_stream(side)
+        cur.wait_stream(side)
+
+    def e2e_step():
+        body()
         iris_kernel.check_errors(dev)  # one host read of the error word per step (syncs)
 
     iris_kernel.set_validation_mode("deferred")
     ms = timed(e2e_step, args.steps, dev, dist, args.warmup)
-    # the same step with each call replayed from a CUDA graph captured once
-    graphs = {n: graph_of(fn, dev) for n, fn in calls.items()}
-    step_calls = dict(calls)
-    calls["dec"], calls["app"] = graphs["dec"].replay, graphs["app"].replay
-    ms_graph = timed(e2e_step, args.steps, dev, dist, args.warmup)
-    calls.update(step_calls)
-    del graphs
+    # the same step (copies, calls, output copy) captured once in a CUDA graph and replayed
+    g_e2e = graph_of(body, dev)
+
+    def e2e_graph_step():
+        g_e2e.replay()
+        iris_kernel.check_errors(dev)
+
+    ms_graph = timed(e2e_graph_step, args.steps, dev, dist, args.warmup)
+    del g_e2e
     iris_kernel.set_validation_mode("sync")
     ms = reduce_over_ranks(ms, dist, dev)
     ms_graph = reduce_over_ranks(ms_graph, dist, dev)
