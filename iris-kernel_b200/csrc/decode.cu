@@ -1660,14 +1660,18 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const D
   const int n = static_cast<int>(l - f + 1);
   const int64_t rec_first = f * 2 + (ps > range_start(f, U, R) ? 1 : 0);
   constexpr int kQuads = D / 4;
-  // T adjacent lanes share one (query head, 4 dims) item: lane j of the group
-  // merges records j, j + T, j + 2T, ... (eight per load round), then the
-  // group combines its partial merges with shuffles.  Sequences split over
-  // many ranges (small batches) thus need one or two load rounds, not n / 8.
+  // T lanes of a warp share one (query head, 4 dims) item: lane j of the
+  // group merges records j, j + T, j + 2T, ... (eight per load round), then
+  // the group combines its partial merges with shuffles.  Sequences split
+  // over many ranges (small batches) thus need one or two load rounds, not
+  // n / 8.  A warp holds G = 32 / T items and the lanes of one item are G
+  // apart, so the G lanes of each record's load read adjacent quads of one
+  // record (G * 16 contiguous bytes).
   const int T = p.combine_lanes;
+  const int G = 32 / T;
   const int items = p.hq * kQuads;
-  const int slot = blockIdx.y * blockDim.x + threadIdx.x;
-  const int item = slot / T, j = slot % T;
+  const int lane = threadIdx.x & 31;
+  const int item = ((blockIdx.y * blockDim.x + threadIdx.x) >> 5) * G + lane % G, j = lane / G;
   const bool valid = item < items;
   const int qh = item / kQuads, t = item % kQuads;
   float m = kNegInf, wsum = 0.f;
@@ -1709,8 +1713,8 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const D
       m = mc;
     }
   }
-  // the group's lanes are adjacent (T divides 32): combine their partial merges
-  for (int o = 1; o < T; o <<= 1) {
+  // combine the group's partial merges (its lanes are G apart)
+  for (int o = G; o < 32; o <<= 1) {
     const float mo = __shfl_xor_sync(0xffffffffu, m, o);
     const float wo = __shfl_xor_sync(0xffffffffu, wsum, o);
     const float ax = __shfl_xor_sync(0xffffffffu, acc.x, o), ay = __shfl_xor_sync(0xffffffffu, acc.y, o);
