@@ -22,8 +22,10 @@ and ``scaling`` is "strong"; ``value`` is the whole batch's algorithmic bytes
 read, output written, block table; append: fp16 K/V read, packed bytes and
 scales written, slots/positions and one RoPE row) / step time, in TB/s, with
 inputs resident in HBM; the step is replayed from a CUDA graph (validation in
-deferred mode, no host syncs).  Inputs (303 MB per step at N=1) exceed the
-126 MB L2, so no flush is needed between steps.
+deferred mode, no host syncs).  Inputs (303 MB per step at N=1) exceed
+twice the 126 MB L2, so no flush is needed between steps.  A GPU whose share
+is under twice the L2 (config 2 at N >= 2, config 3 at N = 8, config 5a)
+times its steps one by one, each after a 256 MB write that evicts the L2.
 ``e2e``: the same metric through the public Python API with host buffers:
 per step the new query / K / V / positions / slots are copied from pinned
 host memory, the decode and append calls run, the fp16 output is copied
@@ -367,24 +369,60 @@ def graph_of(fn, dev):
     return gr
 
 
-def timed(fn, steps, dev, dist, warmup):
+L2_BYTES = 126 * 2**20
+FLUSH_BYTES = 256 * 2**20
+
+
+class L2Flush:
+    """Evicts the L2 between timed steps: a 256 MB write (twice the L2)."""
+
+    def __init__(self, dev):
+        self.buf = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def __call__(self):
+        self.buf.zero_()
+
+
+def needs_flush(step_bytes):
+    """A step whose inputs on one GPU are under twice the L2 would find them
+    there from the previous step: such steps are timed one by one with the
+    L2 flushed in between."""
+    return step_bytes < 2 * L2_BYTES
+
+
+def timed(fn, steps, dev, dist, warmup, flush=None):
     """Warm up, barrier + sync, time exactly `steps` calls with CUDA events
-    on the current stream, barrier + sync; returns ms for all steps."""
+    on the current stream, barrier + sync; returns ms for all steps.  With
+    `flush`, every call (warm-up included) follows an L2 flush, and each call
+    is timed between its own events, so the flushes are not counted."""
     for _ in range(warmup):
+        if flush is not None:
+            flush()
         fn()
     torch.cuda.synchronize(dev)
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    st.record()
-    for _ in range(steps):
-        fn()
-    en.record()
-    torch.cuda.synchronize(dev)
+    if flush is None:
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st.record()
+        for _ in range(steps):
+            fn()
+        en.record()
+        torch.cuda.synchronize(dev)
+        total = st.elapsed_time(en)
+    else:
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for st, en in evs:
+            flush()
+            st.record()
+            fn()
+            en.record()
+        torch.cuda.synchronize(dev)
+        total = sum(st.elapsed_time(en) for st, en in evs)
     if dist is not None:
         dist.barrier()
-    return st.elapsed_time(en)
+    return total
 
 
 def reduce_over_ranks(x, dist, dev, op="max"):
@@ -642,11 +680,16 @@ METRIC = "decode-attn achieved HBM TB/s (% of B200 peak) + us/step; append token
 
 
 def _config(world):
+    nseq = B // world if B % world == 0 else -(-B // world)
+    mb = (decode_bytes(nseq) + append_bytes(nseq)) / 1e6
     return {"workload": "BASELINE config 2: INT4 paged decode 64 x 4096 (Hq 32, Hkv 8, D 128) + 1-token append",
             "batch": B, "context": L, "page_size": P, "group": G,
             "parallelism": f"sequence-sharded {B // world if B % world == 0 else '~' + str(B // world)} seqs/GPU"
                            if world > 1 else "one GPU",
-            "l2": "no flush: 303 MB of cache per step > 126 MB L2"}
+            "l2": (f"flushed: {mb:.0f} MB of cache per GPU per step < 2 x 126 MB L2, so every timed step follows "
+                   "a 256 MB write and is timed between its own events"
+                   if needs_flush(decode_bytes(nseq) + append_bytes(nseq))
+                   else f"no flush: {mb:.0f} MB of cache per GPU per step > 2 x 126 MB L2")}
 
 
 # ------------------------------------------------------------- config 4 pieces
@@ -785,6 +828,8 @@ def main():
     # ---- config 2 step: value (graph replay, inputs resident) ----
     lo, hi = shard(world, rank)
     nseq = hi - lo
+    # this GPU's share of the step under twice the L2: flush between timed steps
+    c2_flush = L2Flush(dev) if needs_flush(decode_bytes(nseq) + append_bytes(nseq)) else None
     if run("c2"):
         w = build_c2(dev, 1234 + rank, nseq)
 
@@ -813,17 +858,17 @@ def main():
         g_dec = graph_of(step_decode, dev)
         g_app = graph_of(step_append, dev)
         clk = Clocks(local).__enter__()
-        ms = timed(g_step.replay, args.steps, dev, dist, args.warmup)
+        ms = timed(g_step.replay, args.steps, dev, dist, args.warmup, c2_flush)
         d_steps = max(args.steps, 200)
-        ms_dec = timed(g_dec.replay, d_steps, dev, dist, args.warmup) / d_steps
-        ms_app = timed(g_app.replay, d_steps, dev, dist, args.warmup) / d_steps
+        ms_dec = timed(g_dec.replay, d_steps, dev, dist, args.warmup, c2_flush) / d_steps
+        ms_app = timed(g_app.replay, d_steps, dev, dist, args.warmup, c2_flush) / d_steps
         iris_kernel.check_errors(dev)
         del g_step, g_dec, g_app
         ms = reduce_over_ranks(ms, dist, dev)
         dec_us = reduce_over_ranks(ms_dec, dist, dev) * 1e3
         app_us = reduce_over_ranks(ms_app, dist, dev) * 1e3
         step_ms = ms / args.steps
-        e2e = run_e2e(w, args, dev, dist, world)
+        e2e = run_e2e(w, args, dev, dist, world, c2_flush)
         clk.__exit__(None, None, None)
         clocks = clk.summary()
         del w
@@ -846,7 +891,9 @@ def main():
         g_a5 = graph_of(lambda: fused_rope_int4_paged_append(x5["k"], x5["v"], x5["pos"], x5["slots"], x5["cos"],
                                                              x5["sin"], x5["kd"], x5["vd"], x5["ks"], x5["vs"],
                                                              rotary_dim=D, page_size=P), dev)
-        a5_us = reduce_over_ranks(timed(g_a5.replay, x_steps, dev, dist, args.warmup), dist, dev) / x_steps * 1e3
+        a5_flush = L2Flush(dev) if needs_flush(A5_BYTES) else None
+        a5_us = reduce_over_ranks(timed(g_a5.replay, x_steps, dev, dist, args.warmup, a5_flush), dist, dev) / x_steps * 1e3
+        del a5_flush
         iris_kernel.check_errors(dev)
         del g_a5, x5
         extra["c5a"] = {"us": a5_us, "tokens_per_s": world * A5_T / (a5_us * 1e-6)}
@@ -907,7 +954,9 @@ def main():
         iris_kernel.set_validation_mode("deferred")
         g_c3 = graph_of(lambda: fused_int4_paged_decode_attention(c3["q"], c3["kd"], c3["vd"], c3["ks"], c3["vs"],
                                                                   c3["bt"], c3["lens"], c3["out"]), dev)
-        c3_us = reduce_over_ranks(timed(g_c3.replay, x_steps, dev, dist, args.warmup), dist, dev) / x_steps * 1e3
+        c3_flush = L2Flush(dev) if needs_flush(c3["bytes"]) else None
+        c3_us = reduce_over_ranks(timed(g_c3.replay, x_steps, dev, dist, args.warmup, c3_flush), dist, dev) / x_steps * 1e3
+        del c3_flush
         iris_kernel.check_errors(dev)
         extra["c3"] = {"us": c3_us, "tbs": c3["total_bytes"] / (c3_us * 1e-6) / 1e12,
                        "frac": c3["total_bytes"] / (c3_us * 1e-6) / 1e9 / (world * peak)}
@@ -974,7 +1023,7 @@ def _round(d):
     return d
 
 
-def run_e2e(w, args, dev, dist, world):
+def run_e2e(w, args, dev, dist, world, flush=None):
     """The step through the public Python API with host buffers (deferred
     validation, the step's error word read on the host once per step).  The
     query copy leads and the decode starts as soon as it has landed, the
@@ -1029,7 +1078,7 @@ def run_e2e(w, args, dev, dist, world):
         iris_kernel.check_errors(dev)  # one host read of the error word per step (syncs)
 
     iris_kernel.set_validation_mode("deferred")
-    ms = timed(e2e_step, args.steps, dev, dist, args.warmup)
+    ms = timed(e2e_step, args.steps, dev, dist, args.warmup, flush)
     # the same step (copies, calls, output copy) captured once in a CUDA graph and replayed
     g_e2e = graph_of(body, dev)
 
@@ -1037,7 +1086,7 @@ def run_e2e(w, args, dev, dist, world):
         g_e2e.replay()
         iris_kernel.check_errors(dev)
 
-    ms_graph = timed(e2e_graph_step, args.steps, dev, dist, args.warmup)
+    ms_graph = timed(e2e_graph_step, args.steps, dev, dist, args.warmup, flush)
     del g_e2e
     iris_kernel.set_validation_mode("sync")
     ms = reduce_over_ranks(ms, dist, dev)
