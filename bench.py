@@ -757,9 +757,9 @@ def c4_self_check(c4, dec4, out, dist, rank, world, dev):
 
 def c4_breakdown(c4, dec4, steps, dev, dist, warmup):
     """Per-stage device times of the split-context step, each stage replayed
-    from its own graph: the local LSE decode (into the exchange buffer for
-    the NVLink transport), then the peer-memory merge, or for NCCL the
-    all-gather and the merge.  Returns max-over-ranks us per step of each, and the min over ranks
+    from its own graph: the local LSE decode, then the peer-memory merge
+    (which publishes the partial), or for NCCL the all-gather and the
+    merge.  Returns max-over-ranks us per step of each, and the min over ranks
     of the decode (the spread is the rank skew the exchange absorbs)."""
     from iris_kernel.fused_attention import decode_partial, merge_lse_packed
 
@@ -778,7 +778,8 @@ def c4_breakdown(c4, dec4, steps, dev, dist, warmup):
 
     stages = [("decode", dec)]
     if dec4.xchg is not None:
-        stages += [("p2p_merge", lambda: dec4.xchg.merge(dec4.output.view(-1, D)))]
+        stages += [("p2p_merge", lambda: dec4.xchg.merge(dec4.output.view(-1, D), dec4._o.view(-1, D),
+                                                          dec4._lse.view(-1)))]
     else:
         stages += [("merge", merge)] + ([("allgather", gather)] if dist is not None else [])
     res = {}

@@ -308,26 +308,22 @@ IRIS_API int iris_b200_merge_lse_packed(const float* parts, int32_t num_parts, i
  * No counterpart in the reference (single GPU). In split-context decode each
  * GPU computes, for the whole batch, a log-sum-exp partial (IRIS_DECODE_OUT_LSE:
  * O [rows, D] fp32, lse [rows] fp32, rows = B*Hq) over its own context splits;
- * every GPU needs their merge. These calls replace an all-gather + merge: each
- * GPU writes its partial into its exchange buffer, which the other GPUs have
- * mapped (CUDA IPC), and one merge kernel per GPU and step reads every GPU's
- * partial straight from its memory over NVLink.
+ * every GPU needs their merge. These calls replace an all-gather + merge: one
+ * kernel per GPU and step publishes this GPU's partial in its exchange buffer,
+ * which the other GPUs have mapped (CUDA IPC), and merges every GPU's partial
+ * read straight from its memory over NVLink.
  *
- * Exchange buffer: IRIS_XCHG_HEADER_BYTES of header (flags; the library's),
- * then the partial: O [rows, head_dim] fp32 at offset IRIS_XCHG_HEADER_BYTES,
- * lse [rows] fp32 right after it. Per step, every GPU (1) writes its partial
- * there with any kernel on the stream (the LSE decode writes it directly),
- * then (2) calls iris_b200_xchg_merge on the same stream. The merge marks the
- * partial complete, waits for every other GPU's, merges, and before it ends
- * waits until every other GPU has read this GPU's partial, so the next step's
- * write in (1) never races a reader. All GPUs run the same steps in the same
- * order. Waits are bounded: a GPU that does not arrive within limit_ns sets
- * IRIS_ERR_PIPELINE_TIMEOUT, after which the exchange must be rebuilt.
+ * Per step every GPU calls iris_b200_xchg_merge once, after the kernel that
+ * wrote its partial, on the same stream; all GPUs run the same steps in the
+ * same order. The buffer holds two slots used on alternate steps, so a step
+ * never waits for the others to finish reading. Waits are bounded: a GPU that
+ * does not arrive within limit_ns sets IRIS_ERR_PIPELINE_TIMEOUT, after which
+ * the exchange must be rebuilt.
  */
 #define IRIS_IPC_HANDLE_BYTES 64
 #define IRIS_XCHG_HEADER_BYTES 256
 
-/* Bytes of one GPU's exchange buffer (header + partial); 0 for a bad shape. */
+/* Bytes of one GPU's exchange buffer (header + two slots); 0 for a bad shape. */
 IRIS_API size_t iris_b200_xchg_buffer_bytes(int64_t rows, int32_t head_dim);
 
 /* Allocate (cudaMalloc, so that its IPC handle covers exactly it) and zero an
@@ -341,15 +337,16 @@ IRIS_API int iris_b200_ipc_export(const void* buf, void* handle);
 IRIS_API int iris_b200_ipc_open(const void* handle, void** peer_buf);
 IRIS_API int iris_b200_ipc_close(void* peer_buf);
 
-/* One step's merge on GPU my_rank: mark this GPU's partial complete, wait
- * (bounded by limit_ns) for every GPU's, merge all num_ranks partials into
- * output [rows, head_dim] fp16, then wait until the other GPUs have read this
- * GPU's partial. bufs: host array of num_ranks (<= 8) device addresses, this
- * GPU's buffer at my_rank and the mapped peer buffers elsewhere. A part whose
- * lse is -inf for a row (no tokens of that sequence) is skipped. */
+/* One step's merge on GPU my_rank: publish this GPU's partial (local_o [rows,
+ * head_dim] fp32, 16-byte aligned; local_lse [rows] fp32), wait (bounded by
+ * limit_ns) for every GPU's, and merge all num_ranks partials into output
+ * [rows, head_dim] fp16. bufs: host array of num_ranks (<= 8) device
+ * addresses, this GPU's buffer at my_rank and the mapped peer buffers
+ * elsewhere. A part whose lse is -inf for a row (no tokens of that sequence)
+ * is skipped. A cooperative launch of at most one CTA per SM. */
 IRIS_API int iris_b200_xchg_merge(void* const* bufs, int32_t num_ranks, int32_t my_rank, int64_t rows,
-                                  int32_t head_dim, void* output, int32_t* error_word, int64_t limit_ns,
-                                  void* stream);
+                                  int32_t head_dim, const float* local_o, const float* local_lse, void* output,
+                                  int32_t* error_word, int64_t limit_ns, void* stream);
 
 #ifdef __cplusplus
 }

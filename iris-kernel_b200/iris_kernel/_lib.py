@@ -72,8 +72,8 @@ SIGNATURES = {
     "iris_b200_ipc_export": (ctypes.c_int, [_c_p, _c_p]),
     "iris_b200_ipc_open": (ctypes.c_int, [_c_p, ctypes.POINTER(_c_p)]),
     "iris_b200_ipc_close": (ctypes.c_int, [_c_p]),
-    "iris_b200_xchg_merge": (ctypes.c_int, [ctypes.POINTER(_c_p), _c_i32, _c_i32, _c_i64, _c_i32, _c_p, _c_p, _c_i64,
-                                            _c_p]),
+    "iris_b200_xchg_merge": (ctypes.c_int, [ctypes.POINTER(_c_p), _c_i32, _c_i32, _c_i64, _c_i32, _c_p, _c_p, _c_p,
+                                            _c_p, _c_i64, _c_p]),
 }
 
 IPC_HANDLE_BYTES = 64  # IRIS_IPC_HANDLE_BYTES

@@ -180,10 +180,11 @@ class PeerExchange:
     """Split-context merge over NVLink peer memory for one GPU of a process
     group: an exchange buffer on this GPU, mapped by every other GPU of the
     group (CUDA IPC handles swapped over the group once), and the mapped
-    addresses of theirs.  Per step every GPU writes its LSE-form partial into
-    :attr:`o` ``[rows, D]`` and :attr:`lse` ``[rows]`` (fp32 tensors over its
-    own buffer; the decode writes them directly), then calls :meth:`merge`;
-    both are CUDA-graph capturable.  A GPU that does not arrive within
+    addresses of theirs.  Per step every GPU calls :meth:`merge` with its
+    LSE-form partial (``o [rows, D]``, ``lse [rows]`` fp32): one kernel
+    publishes it in this GPU's buffer and merges every GPU's (CUDA-graph
+    capturable; two slots on alternate steps, so no step waits for the
+    others to finish reading).  A GPU that does not arrive within
     ``limit_s`` makes the merge record a pipeline timeout (raised as
     RuntimeError) instead of waiting forever; the exchange must then be
     rebuilt.  Call :meth:`close` on every GPU (it synchronises the group)
@@ -205,9 +206,6 @@ class PeerExchange:
         buf = ctypes.c_void_p()
         _lib.check_status(lib.iris_b200_xchg_alloc(nbytes, ctypes.byref(buf)), "iris_b200_xchg_alloc")
         self.buf = buf.value
-        self.partial = _device_floats(self.buf + _lib.XCHG_HEADER_BYTES, rows * (head_dim + 1), self.device)
-        self.o = self.partial[:rows * head_dim].view(rows, head_dim)
-        self.lse = self.partial[rows * head_dim:]
         self.peers: list[int] = []
         ptrs = []
         if self.world > 1:
@@ -228,14 +226,14 @@ class PeerExchange:
             ptrs.append(self.buf)
         self.bufs = (ctypes.c_void_p * self.world)(*ptrs)
 
-    def merge(self, output: torch.Tensor) -> torch.Tensor:
-        """Merge every GPU's partial of this step into ``output [rows, D]``
-        fp16 (this GPU's partial must be in :attr:`o` / :attr:`lse`, written
-        earlier on the current stream)."""
+    def merge(self, output: torch.Tensor, o: torch.Tensor, lse: torch.Tensor) -> torch.Tensor:
+        """Publish this GPU's partial of the step (``o [rows, D]``, ``lse
+        [rows]`` fp32, contiguous, written earlier on the current stream) and
+        merge every GPU's into ``output [rows, D]`` fp16."""
         word = _runtime.error_word(self.device)
         _lib.check_status(
-            _lib.lib.iris_b200_xchg_merge(self.bufs, self.world, self.rank, self.rows, self.head_dim,
-                                          output.data_ptr(), word.data_ptr(), self.limit_ns,
+            _lib.lib.iris_b200_xchg_merge(self.bufs, self.world, self.rank, self.rows, self.head_dim, o.data_ptr(),
+                                          lse.data_ptr(), output.data_ptr(), word.data_ptr(), self.limit_ns,
                                           _runtime.stream_ptr(self.device)),
             "iris_b200_xchg_merge")
         if _runtime.validation_mode() == "sync":
@@ -248,7 +246,6 @@ class PeerExchange:
         if self.buf is None:
             return
         torch.cuda.synchronize(self.device)
-        self.partial = self.o = self.lse = None  # views of the buffer freed below
         for p in self.peers:
             _lib.lib.iris_b200_ipc_close(p)
         self.peers = []
@@ -290,9 +287,8 @@ class SplitContextDecoder:
         self.transport = transport
         n = packed_size(plan.batch, num_q_heads, head_dim)
         if transport == "p2p":
-            # the exchange buffer's partial has the packed layout: the decode writes it directly
             self.xchg = PeerExchange(plan.batch * num_q_heads, head_dim, group=group)
-            self.send, self.recv = self.xchg.partial, None
+            self.send, self.recv = torch.zeros(n, dtype=torch.float32, device=dev), None
         else:
             self.xchg = None
             self.send = torch.zeros(n, dtype=torch.float32, device=dev)
@@ -309,7 +305,6 @@ class SplitContextDecoder:
     def close(self) -> None:
         """Release the peer exchange (every GPU of the group must call it)."""
         if self.xchg is not None:
-            self.send = self._o = self._lse = None  # views of the exchange buffer
             self.xchg.close()
             self.xchg = None
 
@@ -329,7 +324,7 @@ class SplitContextDecoder:
                 self._o.index_copy_(0, self.idx, self._o_l)
                 self._lse.index_copy_(0, self.idx, self._lse_l)
         if self.xchg is not None:
-            self.xchg.merge(self.output.view(-1, self.d))
+            self.xchg.merge(self.output.view(-1, self.d), self._o.view(-1, self.d), self._lse.view(-1))
             return self.output
         if self.world > 1:
             dist.all_gather_into_tensor(self.recv, self.send, group=self.group)

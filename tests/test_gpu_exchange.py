@@ -3,21 +3,19 @@ the ranks emulated with one exchange buffer each.
 
 On one GPU the emulated ranks' merges cannot wait for one another (nothing
 guarantees that separate launches run at the same time), so before each
-step the host sets what the other ranks' merges would have set: every
-buffer's step flag and its count of completed peer reads.  The
-merges then run one after another and none of them waits.  The real
-cross-GPU handshake runs in the two-GPU worker of test_gpu_parallel.py.
+step the host does what the other ranks' merges would have done by then:
+it writes every rank's partial into that rank's slot of the step and raises
+every rank's flag.  The merges then run one after another and none of them
+waits.  The real cross-GPU handshake runs in the two-GPU worker of
+test_gpu_parallel.py.
 
-* Every emulated rank writes its log-sum-exp partial into its buffer; every
-  rank's merge, reading all buffers, equals the FP32 oracle within the
-  decode tolerance, over two steps with different queries, and leaves the
-  header as the protocol says (step counter advanced, one read recorded per
-  peer).
-* A merge whose peer never marks its partial complete gives up after its
-  time limit, records the pipeline-timeout bit and writes nothing; one whose
-  peers never record their reads merges correctly and then records the
-  timeout.  Each wait is on a flag nothing sets, bounded at 20 ms; the
-  context stays usable."""
+* Every emulated rank's merge publishes its own partial and merges all of
+  them; the output equals the FP32 oracle within the decode tolerance, over
+  two steps with different queries (both slots), and the header is left as
+  the protocol says (flag and step counter at the step, arrivals reset).
+* A merge whose peer never publishes gives up after its time limit, records
+  the pipeline-timeout bit and writes nothing (a flag that nothing sets,
+  bounded at 20 ms); the context stays usable."""
 import ctypes
 
 import numpy as np
@@ -30,7 +28,11 @@ from oracle import iris_oracle as orc
 
 pytestmark = pytest.mark.gpu
 
-FLAG, EPOCH, READERS = 0, 8, 16  # header words (int64) of one exchange buffer
+FLAG, EPOCH, COUNT = 0, 8, 16  # header words (int64) of one exchange buffer
+
+
+def _slot_floats(rows, d):
+    return (rows * (d + 1) * 4 + 255) // 256 * 64
 
 
 def _alloc(n, rows, d):
@@ -38,15 +40,16 @@ def _alloc(n, rows, d):
     from iris_kernel.parallel import _device_floats
 
     nbytes = _lib.lib.iris_b200_xchg_buffer_bytes(rows, d)
-    assert nbytes == _lib.XCHG_HEADER_BYTES + rows * (d + 1) * 4
-    bufs, parts, heads = [], [], []
+    assert nbytes == _lib.XCHG_HEADER_BYTES + 2 * _slot_floats(rows, d) * 4
+    bufs, slots, heads = [], [], []
     for _ in range(n):
         p = ctypes.c_void_p()
         assert _lib.lib.iris_b200_xchg_alloc(nbytes, ctypes.byref(p)) == 0
         bufs.append(p.value)
-        parts.append(_device_floats(p.value + _lib.XCHG_HEADER_BYTES, rows * (d + 1), torch.device("cuda")))
+        whole = _device_floats(p.value + _lib.XCHG_HEADER_BYTES, 2 * _slot_floats(rows, d), torch.device("cuda"))
+        slots.append([whole[k * _slot_floats(rows, d):k * _slot_floats(rows, d) + rows * (d + 1)] for k in (0, 1)])
         heads.append(_device_floats(p.value, _lib.XCHG_HEADER_BYTES // 4, torch.device("cuda")).view(torch.int64))
-    return bufs, parts, heads
+    return bufs, slots, heads
 
 
 def _free(bufs):
@@ -74,11 +77,13 @@ def _partial(c, t, world, rank, query):
     return P.pack_partials(o, lse, plan.seqs, B)
 
 
-def _merge(bufs, rank, rows, d, out, err, limit_ns):
+def _merge(bufs, rank, rows, d, part, out, err, limit_ns):
     from iris_kernel import _lib
 
     arr = (ctypes.c_void_p * len(bufs))(*bufs)
-    return _lib.lib.iris_b200_xchg_merge(arr, len(bufs), rank, rows, d, out.data_ptr(), err.data_ptr(), limit_ns,
+    n = rows * d
+    return _lib.lib.iris_b200_xchg_merge(arr, len(bufs), rank, rows, d, part[:n].data_ptr(), part[n:].data_ptr(),
+                                         out.data_ptr(), err.data_ptr(), limit_ns,
                                          torch.cuda.current_stream().cuda_stream)
 
 
@@ -87,32 +92,31 @@ def test_exchange_merge_matches_oracle_two_steps(world):
     c = cases.decode_random(seed=400 + world, B=6, Hq=32, Hkv=8, D=128, lens=[1000, 1, 333, 16, 2049, 700])
     t = to_dev(c, cases.DECODE_KEYS)
     B, Hq, D = t["query"].shape
-    bufs, parts, heads = _alloc(world, B * Hq, D)
+    rows = B * Hq
+    bufs, slots, heads = _alloc(world, rows, D)
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     try:
         for e in (1, 2):
             q = t["query"] if e == 1 else (t["query"].float() * -0.7).half()
-            for r in range(world):
-                parts[r].copy_(_partial(c, t, world, r, q))
+            parts = [_partial(c, t, world, r, q) for r in range(world)]
             cc = dict(c)
             cc["query"] = q.cpu().numpy()
             ref = orc.decode_attention(*[cc[k] for k in cases.DECODE_KEYS])
             torch.cuda.synchronize()
-            for h in heads:  # what the other ranks' merges would have set by now
-                h[FLAG] = e
-                h[READERS] = (world - 1) * e
+            for r in range(world):  # what every rank's merge publishes at step e
+                slots[r][e & 1].copy_(parts[r])
+                heads[r][FLAG] = e
             for r in range(world):
                 out = torch.full((B, Hq, D), float("nan"), dtype=torch.float16, device="cuda")
-                assert _merge(bufs, r, B * Hq, D, out, err, 2_000_000_000) == 0
+                assert _merge(bufs, r, rows, D, parts[r], out, err, 2_000_000_000) == 0
                 torch.cuda.synchronize()
                 assert int(err.item()) == 0
                 assert_decode_close(out, ref)
-                assert int(heads[r][EPOCH]) == e  # the merge advanced this rank's step counter
-            torch.cuda.synchronize()
-            for r in range(world):  # every peer recorded one read of each rank's partial
-                assert int(heads[r][READERS]) == (world - 1) * e + (world - 1)
+                assert int(heads[r][EPOCH]) == e and int(heads[r][FLAG]) == e
+                assert int(heads[r][COUNT]) & 0xFFFFFFFF == 0  # arrivals reset for the next step
+                assert torch.equal(slots[r][e & 1], parts[r])  # the merge published this rank's partial
     finally:
-        del parts, heads
+        del slots, heads
         _free(bufs)
 
 
@@ -123,33 +127,23 @@ def test_exchange_merge_times_out_when_a_peer_never_arrives():
     c = cases.decode_random(seed=410, B=2, Hq=8, Hkv=2, D=64, lens=[100, 40])
     t = to_dev(c, cases.DECODE_KEYS)
     B, Hq, D = t["query"].shape
-    bufs, parts, heads = _alloc(2, B * Hq, D)
+    bufs, slots, heads = _alloc(2, B * Hq, D)
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     ref = orc.decode_attention(*[c[k] for k in cases.DECODE_KEYS])
     try:
-        for r in range(2):
-            parts[r].copy_(_partial(c, t, 2, r, t["query"]))
+        part = _partial(c, t, 2, 0, t["query"])
         torch.cuda.synchronize()
-        # rank 1 never marks its partial complete: rank 0 gives up before merging
+        # rank 1 never publishes: rank 0 publishes, then gives up before merging
         out = torch.full((B, Hq, D), float("nan"), dtype=torch.float16, device="cuda")
-        assert _merge(bufs, 0, B * Hq, D, out, err, 20_000_000) == 0  # 20 ms limit
+        assert _merge(bufs, 0, B * Hq, D, part, out, err, 20_000_000) == 0  # 20 ms limit
         torch.cuda.synchronize()
         assert int(err.item()) & _lib.ERR_PIPELINE_TIMEOUT
         assert bool(torch.isnan(out).all())  # nothing written
-        assert int(heads[0][FLAG]) == 1 and int(heads[0][EPOCH]) == 0
-        # rank 1's partial is complete but rank 1 never reads rank 0's: the merge is
-        # right, then its wait for the read runs out
-        err.zero_()
-        heads[1][FLAG] = 1
-        assert _merge(bufs, 0, B * Hq, D, out, err, 20_000_000) == 0
-        torch.cuda.synchronize()
-        assert int(err.item()) & _lib.ERR_PIPELINE_TIMEOUT
-        assert_decode_close(out, ref)
-        assert int(heads[1][READERS]) == 1 and int(heads[0][READERS]) == 0
+        assert int(heads[0][FLAG]) == 1 and int(heads[1][FLAG]) == 0
         # the context is still usable: a regular decode right after is correct
         got = fused_int4_paged_decode_attention(*[t[k] for k in cases.DECODE_KEYS])
         torch.cuda.synchronize()
         assert_decode_close(got, ref)
     finally:
-        del parts, heads
+        del slots, heads
         _free(bufs)
