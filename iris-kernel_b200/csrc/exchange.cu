@@ -76,9 +76,9 @@ __host__ __device__ inline size_t slot_bytes(int64_t rows, int32_t head_dim) {
 }
 
 // One warp per row, 4 dims per lane and step; NR (the number of GPUs, a
-// compile-time constant) lets every GPU's loads of a row issue together, so a
-// row costs one NVLink round trip for its lse values and one for its O
-// values.  A part with lse = -inf holds none of the row's tokens and is
+// compile-time constant) lets every GPU's loads of a row issue together, and
+// the first 128 dims' O values are loaded with the lse values, so a row of
+// head_dim <= 128 costs one NVLink round trip.  A part with lse = -inf holds none of the row's tokens and is
 // skipped (its O may hold anything).
 template <int NR>
 __global__ void __launch_bounds__(kXchgThreads) xchg_merge_kernel(Peers peers, int32_t me, int64_t rows,
@@ -130,17 +130,23 @@ __global__ void __launch_bounds__(kXchgThreads) xchg_merge_kernel(Peers peers, i
   for (int64_t row = static_cast<int64_t>(blockIdx.x) * warps + warp; row < rows;
        row += static_cast<int64_t>(gridDim.x) * warps) {
     float lse[NR];
+    float4 v[NR];
 #pragma unroll
-    for (int k = 0; k < NR; ++k) lse[k] = __ldcv(reinterpret_cast<const float*>(peers.buf[k] + slot) + n_o + row);
+    for (int k = 0; k < NR; ++k) {
+      const float* part = reinterpret_cast<const float*>(peers.buf[k] + slot);
+      lse[k] = __ldcv(part + n_o + row);
+      if (4 * lane < head_dim) v[k] = __ldcv(reinterpret_cast<const float4*>(part + row * head_dim + 4 * lane));
+    }
     float mx = kNegInf;
 #pragma unroll
     for (int k = 0; k < NR; ++k) mx = fmaxf(mx, lse[k]);
     for (int d = 4 * lane; d < head_dim; d += 128) {
-      float4 v[NR];
+      if (d != 4 * lane) {
 #pragma unroll
-      for (int k = 0; k < NR; ++k)
-        v[k] = __ldcv(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(peers.buf[k] + slot) +
-                                                      row * head_dim + d));
+        for (int k = 0; k < NR; ++k)
+          v[k] = __ldcv(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(peers.buf[k] + slot) +
+                                                        row * head_dim + d));
+      }
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
       float ws = 0.f;
 #pragma unroll
