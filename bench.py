@@ -25,7 +25,8 @@ inputs resident in HBM; the step is replayed from a CUDA graph (validation in
 deferred mode, no host syncs).  Inputs (303 MB per step at N=1) exceed
 twice the 126 MB L2, so no flush is needed between steps.  A GPU whose share
 is under twice the L2 (config 2 at N >= 2, config 3 at N = 8, config 5a)
-times its steps one by one, each after a 256 MB write that evicts the L2.
+times its steps one by one, each after a 256 MB write and a 256 MB read of
+another buffer that evict the L2 (the read leaves clean lines behind).
 ``e2e``: the same metric through the public Python API with host buffers:
 per step the new query / K / V / positions / slots are copied from pinned
 host memory, the decode and append calls run, the fp16 output is copied
@@ -374,13 +375,17 @@ FLUSH_BYTES = 256 * 2**20
 
 
 class L2Flush:
-    """Evicts the L2 between timed steps: a 256 MB write (twice the L2)."""
+    """Evicts the L2 between timed steps: a 256 MB write (twice the L2), then
+    a 256 MB read of another buffer, so that the L2 holds clean lines and the
+    next step does not pay for writing the flush's dirty lines back."""
 
     def __init__(self, dev):
         self.buf = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        self.rd = torch.zeros(FLUSH_BYTES // 8, dtype=torch.int64, device=dev)
 
     def __call__(self):
         self.buf.zero_()
+        self.rd.sum()
 
 
 def needs_flush(step_bytes):
@@ -687,7 +692,7 @@ def _config(world):
             "parallelism": f"sequence-sharded {B // world if B % world == 0 else '~' + str(B // world)} seqs/GPU"
                            if world > 1 else "one GPU",
             "l2": (f"flushed: {mb:.0f} MB of cache per GPU per step < 2 x 126 MB L2, so every timed step follows "
-                   "a 256 MB write and is timed between its own events"
+                   "a 256 MB write and a 256 MB read of another buffer and is timed between its own events"
                    if needs_flush(decode_bytes(nseq) + append_bytes(nseq))
                    else f"no flush: {mb:.0f} MB of cache per GPU per step > 2 x 126 MB L2")}
 
