@@ -35,7 +35,8 @@ first and the decode starts as soon as it lands; the K/V copy and the
 append run on a second stream meanwhile.
 
 Also reported: config 5b prefill append, config 5a decode-style append,
-config 4 split-context decode over the ranks (one NCCL all-gather per step,
+config 4 split-context decode over the ranks (merged over NVLink peer memory
+at N > 1, the NCCL all-gather path timed beside it,
 with a per-stage breakdown and an FP32 parity self-check on two sequences),
 config 3 sequence-sharded decode, and the matched FP16 decode.
 
@@ -903,7 +904,7 @@ def main():
         iris_kernel.check_errors(dev)
         del g_a5, x5
         extra["c5a"] = {"us": a5_us, "tokens_per_s": world * A5_T / (a5_us * 1e-6)}
-    # ---- config 4: split-context decode over the ranks (one NCCL all-gather per step) ----
+    # ---- config 4: split-context decode over the ranks (peer-memory merge; NCCL beside it) ----
     if run("c4"):
         from iris_kernel import parallel
 

@@ -10,12 +10,12 @@ spreads a decode batch over N GPUs of a node (torch.distributed, NCCL):
   longest first, by token count (the decode's cost is proportional to the
   tokens read, not to the number of sequences).
 
-* Split-context (one all-gather).  Every sequence's context is cut into
+* Split-context (one exchange of partials).  Every sequence's context is cut into
   page-aligned splits of ``split_tokens`` tokens and the splits are dealt out
   to the GPUs (:func:`plan_split_context`); a GPU's cache holds the pages of
   its own splits.  Each GPU runs one log-sum-exp-form decode over the tokens
-  it holds, packs ``(O, lse)`` into one buffer, all-gathers it, and merges the
-  N partials (:func:`split_context_decode`).  A GPU's splits of one sequence
+  it holds, packs ``(O, lse)`` into one buffer, exchanges it, and merges the
+  N partials (:func:`split_context_decode`, :class:`SplitContextDecoder`).  A GPU's splits of one sequence
   are handed to the kernel as a single virtual sequence: attention does not
   depend on the order of the tokens, and only a sequence's final split can end
   in a partly filled page, which the concatenation keeps last.
@@ -25,10 +25,12 @@ partials.  Two transports carry them:
 
 * ``"nccl"``: one ``all_gather_into_tensor`` of the packed partials, then
   the merge kernel;
-* ``"p2p"`` (:class:`PeerExchange`): each GPU's decode writes its partial
-  straight into a buffer the other GPUs have mapped (CUDA IPC), and one merge
-  kernel per GPU reads every partial from its owner's memory over NVLink,
-  with bounded waits on per-GPU step flags (``iris_b200_xchg_*``).
+* ``"p2p"`` (:class:`PeerExchange`): one kernel per GPU and step publishes
+  its partial in a buffer the other GPUs have mapped (CUDA IPC; two slots
+  used on alternate steps) and merges every partial read from its owner's
+  memory over NVLink, with bounded waits on per-GPU step flags
+  (``iris_b200_xchg_*``).  Faster than the all-gather: config 4 at 8 GPUs
+  takes 99.8 us per step against 117.0 us.
 """
 from __future__ import annotations
 
