@@ -1,7 +1,7 @@
 """Benchmark of the INT4 paged KV-cache hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--only all|c2|c3|c4|c5a|c5b|f16] [--no-cpu-baseline]
+                    [--only all|c2|c3|c4|c5a|c5b|f16|next] [--no-cpu-baseline]
 
 Workload (Llama-3-8B shape): 64 sequences x 4096 tokens
 of INT4 paged cache (Hq=32, Hkv=8, D=128, page 16, group 32, pages scattered
@@ -807,7 +807,7 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "tilelang"])
-    ap.add_argument("--only", default="all", choices=["all", "c2", "c3", "c4", "c5a", "c5b", "f16"])
+    ap.add_argument("--only", default="all", choices=["all", "c2", "c3", "c4", "c5a", "c5b", "f16", "next"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -892,6 +892,35 @@ def main():
         extra["c5b"] = {"us": pf_us, "tbs": world * PF_BYTES / (pf_us * 1e-6) / 1e12,
                         "frac": PF_BYTES / (pf_us * 1e-6) / 1e9 / peak,
                         "tokens_per_s": world * PF_S * PF_L / (pf_us * 1e-6)}
+    # ---- the standalone write-path kernels at the config-5b shape (one GPU) ----
+    if run("next") and world == 1:
+        from iris_kernel.fused_kv import fused_quantize_pack_int4, fused_rope_fp16_append
+
+        x = build_prefill(dev, seed=77)
+        T = PF_S * PF_L
+        pk = torch.empty(T, HKV, D // 2, dtype=torch.uint8, device=dev)
+        sc = torch.empty(T, HKV, D // G, dtype=torch.float16, device=dev)
+        iris_kernel.set_validation_mode("deferred")
+        g_q = graph_of(lambda: fused_quantize_pack_int4(x["k"], pk, sc), dev)
+        q_bytes = T * HKV * (2 * D + D // 2 + D // 16)  # fp16 in, packed bytes and scales out
+        q_flush = L2Flush(dev) if needs_flush(q_bytes) else None
+        q_us = timed(g_q.replay, x_steps, dev, None, args.warmup, q_flush) / x_steps * 1e3
+        del g_q, pk, sc, q_flush
+        kc = torch.zeros(T // P, P, HKV, D, dtype=torch.float16, device=dev)
+        vc = torch.zeros_like(kc)
+        g_a = graph_of(lambda: fused_rope_fp16_append(x["k"], x["v"], x["pos"], x["slots"], x["cos"], x["sin"], kc,
+                                                      vc, rotary_dim=D, page_size=P), dev)
+        # K, V fp16 in and out, slots and positions, one cos and one sin row per position
+        a_bytes = T * HKV * 8 * D + T * 8 + PF_L * 2 * (D // 2) * 2
+        a_us = timed(g_a.replay, x_steps, dev, None, args.warmup) / x_steps * 1e3
+        iris_kernel.check_errors(dev)
+        del g_a, kc, vc, x
+        extra["qpack"] = {"us": round(q_us, 2), "tbs": round(q_bytes / (q_us * 1e-6) / 1e12, 3),
+                          "frac": round(q_bytes / (q_us * 1e-6) / 1e9 / peak, 4), "shape": "65536 x 8 x 128",
+                          "l2": "flushed" if needs_flush(q_bytes) else "no flush"}
+        extra["f16_append"] = {"us": round(a_us, 2), "tbs": round(a_bytes / (a_us * 1e-6) / 1e12, 3),
+                               "frac": round(a_bytes / (a_us * 1e-6) / 1e9 / peak, 4),
+                               "tokens_per_s": T / (a_us * 1e-6), "shape": "8 x 8192 tokens, Hkv 8, D 128"}
     if run("c5a"):
         x5 = build_c5a(dev, seed=55 + rank)
         iris_kernel.set_validation_mode("deferred")
