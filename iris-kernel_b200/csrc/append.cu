@@ -561,22 +561,38 @@ struct Fp16AppendParams {
   int64_t num_slots;
   int32_t num_heads, head_dim, rotary_dim;
   int32_t* err;
+  FastDiv row_div;   // thread -> (row, chunk): by threads per row
+  FastDiv head_div;  // row -> (token, head)
 };
 
-template <bool VEC, bool kInline>
+// k32: the launch has fewer than 2^31 threads, so a thread's row, token and
+// head come from 32-bit multiply-shift divisions instead of 64-bit ones.
+template <bool VEC, bool kInline, bool k32>
 __global__ void __launch_bounds__(256) rope_fp16_append_kernel(const Fp16AppendParams p) {
   constexpr int W = VEC ? 8 : 1;  // dims per thread
   const int per_row = p.head_dim / W;
-  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t row = idx / per_row;
+  int64_t row, tok, h;
+  int c;
+  if constexpr (k32) {
+    const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t r32 = p.row_div.div(idx);
+    const uint32_t t32 = p.head_div.div(r32);
+    row = r32;
+    c = static_cast<int>(idx - r32 * static_cast<uint32_t>(per_row));
+    tok = t32;
+    h = r32 - t32 * static_cast<uint32_t>(p.num_heads);
+  } else {
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    row = idx / per_row;
+    c = static_cast<int>(idx - row * per_row);
+    tok = row / p.num_heads;
+    h = row - tok * p.num_heads;
+  }
   bool batch_bad = false;
   if constexpr (kInline)  // a small batch: every CTA validates it (no check kernel before the launch)
     batch_bad = inline_batch_check<256>(p.slots, p.positions, static_cast<int>(p.num_tokens), p.num_slots,
                                         p.max_position, p.err);
   if (row >= p.num_tokens * p.num_heads) return;
-  const int c = static_cast<int>(idx - row * per_row);
-  const int64_t tok = row / p.num_heads;
-  const int64_t h = row - tok * p.num_heads;
   const int32_t slot = __ldg(p.slots + tok);
   if (slot < 0) return;
   const int32_t pos = __ldg(p.positions + tok);
@@ -872,6 +888,9 @@ extern "C" int iris_b200_rope_fp16_paged_append(const void* key, const void* val
   const int threads = 256;
   const int64_t blocks = (threads_total + threads - 1) / threads;
   if (blocks > 0x7fffffffLL) return IRIS_EUNSUPPORTED;
+  const bool k32 = blocks * threads < (1LL << 31);
+  p.row_div = FastDiv::make(static_cast<uint32_t>(vec ? head_dim / 8 : head_dim));
+  p.head_div = FastDiv::make(static_cast<uint32_t>(num_kv_heads));
   clear_stale_cuda_error();
   // programmatic launch: starts while the check kernel before it finishes
   cudaLaunchConfig_t cfg = {};
@@ -885,11 +904,11 @@ extern "C" int iris_b200_rope_fp16_paged_append(const void* key, const void* val
   cfg.attrs = attr;
   const bool small = num_tokens <= kInlineCheckTokens;  // validated inside the kernel, ordinary launch
   cfg.numAttrs = small ? 0 : 1;
-  const cudaError_t e =
-      small ? (vec ? cudaLaunchKernelEx(&cfg, rope_fp16_append_kernel<true, true>, p)
-                   : cudaLaunchKernelEx(&cfg, rope_fp16_append_kernel<false, true>, p))
-            : (vec ? cudaLaunchKernelEx(&cfg, rope_fp16_append_kernel<true, false>, p)
-                   : cudaLaunchKernelEx(&cfg, rope_fp16_append_kernel<false, false>, p));
+  const auto fn = k32 ? (small ? (vec ? rope_fp16_append_kernel<true, true, true> : rope_fp16_append_kernel<false, true, true>)
+                                : (vec ? rope_fp16_append_kernel<true, false, true> : rope_fp16_append_kernel<false, false, true>))
+                      : (small ? (vec ? rope_fp16_append_kernel<true, true, false> : rope_fp16_append_kernel<false, true, false>)
+                               : (vec ? rope_fp16_append_kernel<true, false, false> : rope_fp16_append_kernel<false, false, false>));
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, p);
   if (e != cudaSuccess) {
     record_cuda_error(e, "rope_fp16_append_kernel launch");
     return IRIS_ECUDA;
