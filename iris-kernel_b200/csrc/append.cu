@@ -565,11 +565,13 @@ struct Fp16AppendParams {
   FastDiv head_div;  // row -> (token, head)
 };
 
+// W: dims per thread (16: 32-byte loads, 8: 16-byte loads, 1: scalar).
 // k32: the launch has fewer than 2^31 threads, so a thread's row, token and
 // head come from 32-bit multiply-shift divisions instead of 64-bit ones.
-template <bool VEC, bool kInline, bool k32>
+template <int W, bool kInline, bool k32>
 __global__ void __launch_bounds__(256) rope_fp16_append_kernel(const Fp16AppendParams p) {
-  constexpr int W = VEC ? 8 : 1;  // dims per thread
+  constexpr bool VEC = W >= 8;
+  constexpr int NV = W / 8;  // 16-byte vectors per thread and tensor
   const int per_row = p.head_dim / W;
   int64_t row, tok, h;
   int c;
@@ -612,28 +614,42 @@ __global__ void __launch_bounds__(256) rope_fp16_append_kernel(const Fp16AppendP
   const __half* vrow = p.value + row * p.head_dim;
   const int64_t dst = (static_cast<int64_t>(slot) * p.num_heads + h) * p.head_dim + d0;
   if constexpr (VEC) {
-    uint4 k = ldg_nc_v4(krow + d0);
-    const uint4 v = ldg_nc_v4(vrow + d0);
+    const auto load = [](const __half* src, uint4 (&dst)[NV]) {
+      if constexpr (NV == 2)
+        ldg_nc_v8(src, dst[0], dst[1]);
+      else
+        dst[0] = ldg_nc_v4(src);
+    };
+    uint4 k[NV], v[NV];
+    load(krow + d0, k);
+    load(vrow + d0, v);
     if (d0 < p.rotary_dim) {
       const bool lo = d0 < half;
       const int j = lo ? d0 : d0 - half;  // cos/sin column
-      const uint4 par = ldg_nc_v4(krow + (lo ? d0 + half : d0 - half));
-      const uint4 cs = ldg_nc_v4(p.cos_cache + static_cast<int64_t>(pos) * half + j);
-      const uint4 sn = ldg_nc_v4(p.sin_cache + static_cast<int64_t>(pos) * half + j);
-      __half2* own = reinterpret_cast<__half2*>(&k);
-      const __half2* pr = reinterpret_cast<const __half2*>(&par);
-      const __half2* cc = reinterpret_cast<const __half2*>(&cs);
-      const __half2* ss = reinterpret_cast<const __half2*>(&sn);
+      uint4 par[NV], cs[NV], sn[NV];
+      load(krow + (lo ? d0 + half : d0 - half), par);
+      load(p.cos_cache + static_cast<int64_t>(pos) * half + j, cs);
+      load(p.sin_cache + static_cast<int64_t>(pos) * half + j, sn);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const __half2 pi = lo ? __hneg2(pr[i]) : pr[i];
-        own[i] = __hadd2(__hmul2_rn(own[i], cc[i]), __hmul2_rn(pi, ss[i]));
+      for (int q = 0; q < NV; ++q) {
+        __half2* own = reinterpret_cast<__half2*>(&k[q]);
+        const __half2* pr = reinterpret_cast<const __half2*>(&par[q]);
+        const __half2* cc = reinterpret_cast<const __half2*>(&cs[q]);
+        const __half2* ss = reinterpret_cast<const __half2*>(&sn[q]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const __half2 pi = lo ? __hneg2(pr[i]) : pr[i];
+          own[i] = __hadd2(__hmul2_rn(own[i], cc[i]), __hmul2_rn(pi, ss[i]));
+        }
       }
     }
     grid_dependency_wait();  // the check kernel before this launch has finished
     if (batch_bad || (p.err != nullptr && (*p.err & kRejectBits) != 0)) return;
-    *reinterpret_cast<uint4*>(p.k_cache + dst) = k;
-    *reinterpret_cast<uint4*>(p.v_cache + dst) = v;
+#pragma unroll
+    for (int q = 0; q < NV; ++q) {
+      *reinterpret_cast<uint4*>(p.k_cache + dst + 8 * q) = k[q];
+      *reinterpret_cast<uint4*>(p.v_cache + dst + 8 * q) = v[q];
+    }
   } else {
     __half k = krow[d0];
     const __half v = vrow[d0];
@@ -650,6 +666,15 @@ __global__ void __launch_bounds__(256) rope_fp16_append_kernel(const Fp16AppendP
     p.k_cache[dst] = k;
     p.v_cache[dst] = v;
   }
+}
+
+template <int W>
+static cudaError_t launch_fp16_append(const cudaLaunchConfig_t& cfg, const Fp16AppendParams& p, bool small,
+                                      bool k32) {
+  return k32 ? (small ? cudaLaunchKernelEx(&cfg, rope_fp16_append_kernel<W, true, true>, p)
+                      : cudaLaunchKernelEx(&cfg, rope_fp16_append_kernel<W, false, true>, p))
+             : (small ? cudaLaunchKernelEx(&cfg, rope_fp16_append_kernel<W, true, false>, p)
+                      : cudaLaunchKernelEx(&cfg, rope_fp16_append_kernel<W, false, false>, p));
 }
 
 // L2 prefetch distance of the one-pass kernel in quarters of a resident wave
@@ -884,12 +909,17 @@ extern "C" int iris_b200_rope_fp16_paged_append(const void* key, const void* val
   const bool vec = head_dim % 8 == 0 && rotary_dim % 16 == 0 && aligned(key, 16) && aligned(value, 16) &&
                    aligned(k_cache, 16) && aligned(v_cache, 16) && (rotary_dim == 0 || (aligned(cos_cache, 16) &&
                                                                                         aligned(sin_cache, 16)));
-  const int64_t threads_total = num_tokens * num_kv_heads * (vec ? head_dim / 8 : head_dim);
+  // 32-byte loads when every row, partner and cos / sin chunk of 16 dims is 32-byte aligned
+  const bool wide = vec && head_dim % 16 == 0 && rotary_dim % 32 == 0 && aligned(key, 32) && aligned(value, 32) &&
+                    aligned(k_cache, 32) && aligned(v_cache, 32) &&
+                    (rotary_dim == 0 || (aligned(cos_cache, 32) && aligned(sin_cache, 32))) && append_wide_enabled();
+  const int width = wide ? 16 : vec ? 8 : 1;
+  const int64_t threads_total = num_tokens * num_kv_heads * (head_dim / width);
   const int threads = 256;
   const int64_t blocks = (threads_total + threads - 1) / threads;
   if (blocks > 0x7fffffffLL) return IRIS_EUNSUPPORTED;
   const bool k32 = blocks * threads < (1LL << 31);
-  p.row_div = FastDiv::make(static_cast<uint32_t>(vec ? head_dim / 8 : head_dim));
+  p.row_div = FastDiv::make(static_cast<uint32_t>(head_dim / width));
   p.head_div = FastDiv::make(static_cast<uint32_t>(num_kv_heads));
   clear_stale_cuda_error();
   // programmatic launch: starts while the check kernel before it finishes
@@ -904,11 +934,9 @@ extern "C" int iris_b200_rope_fp16_paged_append(const void* key, const void* val
   cfg.attrs = attr;
   const bool small = num_tokens <= kInlineCheckTokens;  // validated inside the kernel, ordinary launch
   cfg.numAttrs = small ? 0 : 1;
-  const auto fn = k32 ? (small ? (vec ? rope_fp16_append_kernel<true, true, true> : rope_fp16_append_kernel<false, true, true>)
-                                : (vec ? rope_fp16_append_kernel<true, false, true> : rope_fp16_append_kernel<false, false, true>))
-                      : (small ? (vec ? rope_fp16_append_kernel<true, true, false> : rope_fp16_append_kernel<false, true, false>)
-                               : (vec ? rope_fp16_append_kernel<true, false, false> : rope_fp16_append_kernel<false, false, false>));
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, p);
+  const cudaError_t e = width == 16 ? launch_fp16_append<16>(cfg, p, small, k32)
+                        : width == 8   ? launch_fp16_append<8>(cfg, p, small, k32)
+                                       : launch_fp16_append<1>(cfg, p, small, k32);
   if (e != cudaSuccess) {
     record_cuda_error(e, "rope_fp16_append_kernel launch");
     return IRIS_ECUDA;

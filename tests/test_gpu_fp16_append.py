@@ -41,6 +41,32 @@ def test_large_batch_matches_oracle():
         assert t[k].cpu().numpy().tobytes() == ref[k].tobytes()
 
 
+@pytest.mark.parametrize("rotary_dim,shift", [(48, False), (128, True), (128, False), (96, False)])
+def test_every_load_width_matches_oracle(rotary_dim, shift):
+    """The kernel's three forms: 16 dims a thread with 32-byte loads (rotary a
+    multiple of 32, 32-byte aligned bases), 8 dims with 16-byte loads (rotary
+    48, or bases 16 bytes past a 32-byte boundary), byte for byte."""
+    from iris_kernel.fused_kv import fused_rope_fp16_append
+
+    c = cases.fp16_append_case(seed=46 + rotary_dim, T=300, H=4, D=128, rotary_dim=rotary_dim, NP=40)
+    ref = {k: c[k].copy() for k in ("k_cache", "v_cache")}
+    orc.append_fp16(*[c[k] if k not in ref else ref[k] for k in cases.FP16_APPEND_KEYS],
+                    rotary_dim=c["rotary_dim"], page_size=c["page_size"])
+    t = to_dev(c, cases.FP16_APPEND_KEYS)
+    if shift:  # same values, base addresses 16 bytes past a 32-byte boundary
+        for k in ("key", "value", "cos_cache", "sin_cache"):
+            buf = torch.empty(t[k].numel() + 8, dtype=t[k].dtype, device="cuda")
+            y = buf[8:].view(t[k].shape)
+            y.copy_(t[k])
+            assert y.data_ptr() % 32 == 16
+            t[k] = y
+    fused_rope_fp16_append(*[t[k] for k in cases.FP16_APPEND_KEYS], rotary_dim=c["rotary_dim"],
+                           page_size=c["page_size"])
+    torch.cuda.synchronize()
+    for k in ("k_cache", "v_cache"):
+        assert t[k].cpu().numpy().tobytes() == ref[k].tobytes()
+
+
 def test_errors_leave_the_cache_untouched():
     from iris_kernel.fused_kv import fused_rope_fp16_append
 
