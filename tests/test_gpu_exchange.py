@@ -15,7 +15,9 @@ test_gpu_parallel.py.
   the protocol says (flag and step counter at the step, arrivals reset).
 * A merge whose peer never publishes gives up after its time limit, records
   the pipeline-timeout bit and writes nothing (a flag that nothing sets,
-  bounded at 20 ms); the context stays usable."""
+  bounded at 20 ms); the context stays usable.
+* With one process and no process group the decoder's exchange runs its own
+  protocol for real (its only flag is its own), eager and graph-replayed."""
 import ctypes
 
 import numpy as np
@@ -147,3 +149,45 @@ def test_exchange_merge_times_out_when_a_peer_never_arrives():
     finally:
         del slots, heads
         _free(bufs)
+
+
+def test_single_gpu_decoder_over_the_exchange_eager_and_graph():
+    """One process, no process group: the exchange's own protocol end to end
+    on one GPU (its only flag is its own), eager and then replayed from a
+    CUDA graph over several steps, so both slots alternate; every output
+    equals the FP32 oracle."""
+    import iris_kernel
+    from iris_kernel import parallel as P
+
+    c = cases.decode_random(seed=420, B=4, Hq=32, Hkv=8, D=128, lens=[700, 1, 2049, 300])
+    t = to_dev(c, cases.DECODE_KEYS)
+    B, Hq, D = t["query"].shape
+    ref = orc.decode_attention(*[c[k] for k in cases.DECODE_KEYS])
+    plan = P.plan_split_context(c["seq_lens"], 1, 0, split_tokens=256)
+    dec = P.SplitContextDecoder(plan, t["block_table"], Hq, D, transport="p2p")
+    try:
+        for _ in range(3):
+            out = dec(t["query"], t["k_data"], t["v_data"], t["k_scale"], t["v_scale"]).clone()
+            torch.cuda.synchronize()
+            assert_decode_close(out, ref)
+        iris_kernel.set_validation_mode("deferred")
+        try:
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                dec(t["query"], t["k_data"], t["v_data"], t["k_scale"], t["v_scale"])
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                res = dec(t["query"], t["k_data"], t["v_data"], t["k_scale"], t["v_scale"])
+            for _ in range(3):
+                res.zero_()
+                g.replay()
+                torch.cuda.synchronize()
+                iris_kernel.check_errors()
+                assert_decode_close(res, ref)
+            del g
+        finally:
+            iris_kernel.set_validation_mode("sync")
+    finally:
+        dec.close()
