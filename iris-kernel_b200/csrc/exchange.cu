@@ -78,8 +78,8 @@ __host__ __device__ inline size_t slot_bytes(int64_t rows, int32_t head_dim) {
 // One warp per row, 4 dims per lane and step; NR (the number of GPUs, a
 // compile-time constant) lets every GPU's loads of a row issue together, and
 // the first 128 dims' O values are loaded with the lse values, so a row of
-// head_dim <= 128 costs one NVLink round trip.  A part with lse = -inf holds none of the row's tokens and is
-// skipped (its O may hold anything).
+// head_dim <= 128 costs one NVLink round trip.  A part with lse = -inf holds
+// none of the row's tokens and is skipped (its O may hold anything).
 template <int NR>
 __global__ void __launch_bounds__(kXchgThreads) xchg_merge_kernel(Peers peers, int32_t me, int64_t rows,
                                                                   int32_t head_dim, const float* __restrict__ lo,
