@@ -1,7 +1,7 @@
 """Benchmark of the INT4 paged KV-cache hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--only all|c2|c3|c4|c5a|c5b|f16|next] [--no-cpu-baseline]
+                    [--only all|c2|c3|c4|c5a|c5b|f16|next|sweep] [--no-cpu-baseline]
 
 Workload (Llama-3-8B shape): 64 sequences x 4096 tokens
 of INT4 paged cache (Hq=32, Hkv=8, D=128, page 16, group 32, pages scattered
@@ -39,6 +39,11 @@ config 4 split-context decode over the ranks (merged over NVLink peer memory
 at N > 1, the NCCL all-gather path timed beside it,
 with a per-stage breakdown and an FP32 parity self-check on two sequences),
 config 3 sequence-sharded decode, and the matched FP16 decode.
+
+``--only sweep`` (one GPU) prints the reference benchmarks' tables instead:
+INT4 vs matched FP16 decode over L in (128, 512, 2048, 4096) at batch 1 with
+the output cosine and RMSE, and the append over T in (1, 8, 32, 128), each
+beside the reference's torch eager code on the same GPU.
 
 ``--impl reference`` times the reference's own CPU path (its torch eager
 ``torch_eager_int4_paged_decode_attention`` + ``torch_eager_append``, from
@@ -685,6 +690,131 @@ def run_reference(args, dist, rank, world):
 METRIC = "decode-attn achieved HBM TB/s (% of B200 peak) + us/step; append tokens/s"
 
 
+SWEEP_LENS = (128, 512, 2048, 4096)  # the reference's decode sweep (tests/bench_attention.py:291)
+SWEEP_TOKENS = (1, 8, 32, 128)  # the reference's append sweep (tests/bench.py:550)
+
+
+def p50_us(fn, inner, samples=50, warmup=20):
+    """Median over `samples` event-timed runs of `inner` back-to-back calls,
+    per call, in µs (the reference benchmarks' measure, warm L2)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    res = []
+    for _ in range(samples):
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st.record()
+        for _ in range(inner):
+            fn()
+        en.record()
+        en.synchronize()
+        res.append(st.elapsed_time(en) * 1e3 / inner)
+    return statistics.median(res)
+
+
+def _neox(x, cos, sin):
+    """NeoX rotation of the last dimension with fp16 cos/sin rows (set-up only)."""
+    h = x.shape[-1] // 2
+    a, b = x[..., :h].float(), x[..., h:].float()
+    c, s = cos.float(), sin.float()
+    return torch.cat([a * c - b * s, b * c + a * s], dim=-1).half()
+
+
+def run_sweep(args, dev):
+    """The reference benchmarks' two tables on this GPU, one JSON line.
+
+    Decode (batch 1, Hq 32, Hkv 8, D 128, L in SWEEP_LENS): the INT4 and the
+    matched FP16 decode through the public API (deferred validation, calls
+    back to back) and replayed from a graph, the reference's torch eager INT4
+    decode on the same GPU when its install is present, and the INT4 output's
+    cosine and RMSE against the FP16 one.  Both caches are written by this
+    library's appends from the same K/V ~ N(0, 1).
+    Append (Hkv 4, D 128, T in SWEEP_TOKENS new tokens into fresh pages): the
+    INT4 append through the public API and from a graph, and the reference's
+    torch eager append on the same GPU.  The inputs fit in L2 and stay there,
+    as in the reference's benchmarks."""
+    import iris_kernel
+    from iris_kernel.fused_attention import fused_fp16_paged_decode_attention, fused_int4_paged_decode_attention
+    from iris_kernel.fused_kv import fused_rope_fp16_append, fused_rope_int4_paged_append
+
+    ref = load_reference_eager()
+    hq, hkv = 32, 8
+    rows = []
+    iris_kernel.set_validation_mode("deferred")
+    for seq_len in SWEEP_LENS:
+        g = torch.Generator(device=dev).manual_seed(3407 + seq_len)
+        npg = -(-seq_len // P)
+        bt = torch.randperm(npg, generator=g, device=dev).int().view(1, npg).contiguous()
+        lens = torch.full((1,), seq_len, dtype=torch.int32, device=dev)
+        pos = torch.arange(seq_len, dtype=torch.int32, device=dev)
+        slots = (bt[0, pos.long() // P] * P + pos % P).int().contiguous()
+        cos, sin = rope_tables(seq_len, D, dev)
+        k = torch.randn(seq_len, hkv, D, generator=g, device=dev).half()
+        v = torch.randn(seq_len, hkv, D, generator=g, device=dev).half()
+        kd = torch.empty(npg, P, hkv, D // 2, dtype=torch.uint8, device=dev)
+        vd = torch.empty_like(kd)
+        ks = torch.empty(npg, P, hkv, D // G, dtype=torch.float16, device=dev)
+        vs = torch.empty_like(ks)
+        kc = torch.zeros(npg, P, hkv, D, dtype=torch.float16, device=dev)
+        vc = torch.zeros_like(kc)
+        fused_rope_int4_paged_append(k, v, pos, slots, cos, sin, kd, vd, ks, vs, rotary_dim=D, page_size=P)
+        fused_rope_fp16_append(k, v, pos, slots, cos, sin, kc, vc, rotary_dim=D, page_size=P)
+        q = _neox(torch.randn(1, hq, D, generator=g, device=dev).half(), cos[seq_len - 1], sin[seq_len - 1])
+        o4, o16 = torch.empty_like(q), torch.empty_like(q)
+        i4 = lambda: fused_int4_paged_decode_attention(q, kd, vd, ks, vs, bt, lens, o4)
+        f16 = lambda: fused_fp16_paged_decode_attention(q, kc, vc, bt, lens, o16)
+        inner = 50 if seq_len <= 512 else 20
+        row = {"seq_len": seq_len, "int4_us": p50_us(i4, inner), "fp16_us": p50_us(f16, inner)}
+        g4, g16 = graph_of(i4, dev), graph_of(f16, dev)
+        row["int4_graph_us"] = p50_us(g4.replay, inner)
+        row["fp16_graph_us"] = p50_us(g16.replay, inner)
+        del g4, g16
+        if ref is not None:
+            eager = ref["torch_eager_attention"].torch_eager_int4_paged_decode_attention
+            row["eager_int4_us"] = p50_us(lambda: eager(q, kd, vd, ks, vs, bt, lens, page_size=P, group_size=G),
+                                          max(1, inner // 5), samples=20, warmup=3)
+        torch.cuda.synchronize(dev)
+        iris_kernel.check_errors(dev)
+        a, b = o4.float().flatten(0, 1), o16.float().flatten(0, 1)
+        row["vs_fp16"] = row["fp16_us"] / row["int4_us"]
+        row["output_cosine"] = float(torch.nn.functional.cosine_similarity(a, b, dim=-1).mean())
+        row["output_rmse"] = float(((a - b) ** 2).mean().sqrt())
+        rows.append({kk: (round(vv, 4) if isinstance(vv, float) else vv) for kk, vv in row.items()})
+    app_rows = []
+    for tokens in SWEEP_TOKENS:
+        g = torch.Generator(device=dev).manual_seed(11 + tokens)
+        npg = -(-tokens // P)
+        k = torch.randn(tokens, 4, D, generator=g, device=dev).half()
+        v = torch.randn_like(k)
+        pos = torch.arange(tokens, dtype=torch.int32, device=dev)
+        slots = pos.clone()
+        cos, sin = rope_tables(max(tokens, 1), D, dev)
+        kd = torch.empty(npg, P, 4, D // 2, dtype=torch.uint8, device=dev)
+        vd = torch.empty_like(kd)
+        ks = torch.empty(npg, P, 4, D // G, dtype=torch.float16, device=dev)
+        vs = torch.empty_like(ks)
+        ap = lambda: fused_rope_int4_paged_append(k, v, pos, slots, cos, sin, kd, vd, ks, vs, rotary_dim=D,
+                                                  page_size=P)
+        row = {"tokens": tokens, "fused_us": p50_us(ap, 50)}
+        ga = graph_of(ap, dev)
+        row["graph_us"] = p50_us(ga.replay, 50)
+        del ga
+        if ref is not None:
+            eager = ref["torch_eager_kv"].torch_eager_append
+            row["eager_us"] = p50_us(lambda: eager(k, v, pos, slots, cos, sin, kd, vd, ks, vs, rotary_dim=D,
+                                                   group_size=G, page_size=P), 10, samples=20, warmup=3)
+            row["vs_eager"] = row["eager_us"] / row["fused_us"]
+        row["tokens_per_s"] = tokens / (row["fused_us"] * 1e-6)
+        torch.cuda.synchronize(dev)
+        iris_kernel.check_errors(dev)
+        app_rows.append({kk: (round(vv, 4) if isinstance(vv, float) else vv) for kk, vv in row.items()})
+    iris_kernel.set_validation_mode("sync")
+    print(json.dumps({"only": "sweep", "n_gpus": 1, "l2": "warm (inputs fit in L2; calls back to back)",
+                      "decode": rows, "append": app_rows,
+                      "eager": "reference torch eager on this GPU" if ref is not None else "not installed"}),
+          flush=True)
+
+
 def _config(world):
     nseq = B // world if B % world == 0 else -(-B // world)
     mb = (decode_bytes(nseq) + append_bytes(nseq)) / 1e6
@@ -807,7 +937,7 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "tilelang"])
-    ap.add_argument("--only", default="all", choices=["all", "c2", "c3", "c4", "c5a", "c5b", "f16", "next"])
+    ap.add_argument("--only", default="all", choices=["all", "c2", "c3", "c4", "c5a", "c5b", "f16", "next", "sweep"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -826,6 +956,12 @@ def main():
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if args.only == "sweep":  # the reference benchmarks' tables, one GPU, not part of the default run
+        if rank == 0 and world == 1:
+            run_sweep(args, dev)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
     run = (lambda name: args.only in ("all", name))
     x_steps = max(10, min(args.steps, 100))
     peak, peak_kind = _peak_gbs()
