@@ -84,6 +84,7 @@ def _check_scales(query, k_data, v_data, k_scale, v_scale, num_pages, num_kv_hea
 
 
 _OUT_SLOT = 8  # position of the output pointer in the decode entry point's arguments
+_FP16_OUT_SLOT = 6  # the same in the FP16 decode entry point's arguments
 
 
 def _launch(query, k_data, v_data, k_scale, v_scale, block_table, seq_lens, out, out_lse, mode, softmax_scale,
@@ -249,6 +250,15 @@ def fused_fp16_paged_decode_attention(
     fused_attention.py:528-582: same signature, checks and exception types)
     over ``k_cache / v_cache [pages, 16, Hkv, D]`` fp16, with the INT4
     decode's schedule; semantics of torch_eager_fp16_paged_decode_attention."""
+    sig = _runtime.tensor_sig
+    key = ("fp16_decode", sig(query), sig(k_cache), sig(v_cache), sig(block_table), sig(seq_lens),
+           None if output is None else sig(output), page_size, softmax_scale)
+    ent = _runtime.fast_lookup(key)
+    if ent is not None:  # the same signature passed every host check before
+        if output is None:
+            output = torch.empty_like(query)
+        _runtime.fast_run(ent, output.data_ptr())
+        return output
     if k_cache.ndim != 4 or tuple(v_cache.shape) != tuple(k_cache.shape):
         raise ValueError("k_cache/v_cache must have identical rank-4 shapes")
     num_pages, cache_page_size, num_kv_heads, cache_dim = k_cache.shape
@@ -284,16 +294,19 @@ def fused_fp16_paged_decode_attention(
         word = _runtime.error_word(device)
         if not seq_lens.is_contiguous():
             seq_lens = seq_lens.contiguous()
+            key = None  # a fresh copy per call: nothing to reuse
         ws_bytes = _runtime.workspace_bytes(_lib.lib.iris_b200_fp16_decode_workspace_bytes, batch, hq,
                                             num_kv_heads, head_dim, device.index or 0)
         ws = _runtime.scratch(device, stream, "decode_fp16", ws_bytes)
-        _lib.check_status(
-            _lib.lib.iris_b200_fp16_paged_decode(
-                query.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_table.data_ptr(),
+        args = [query.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_table.data_ptr(),
                 block_table.stride(0), seq_lens.data_ptr(), output.data_ptr(), None, _lib.DECODE_OUT_FP16, batch, hq,
                 num_kv_heads, head_dim, num_pages, page_size, block_table.shape[1], scale, ws.data_ptr(), ws.numel(),
-                word.data_ptr(), stream),
-            "iris_b200_fp16_paged_decode")
+                word.data_ptr(), stream]
+        fn = _lib.lib.iris_b200_fp16_paged_decode
+        _lib.check_status(fn(*args), "iris_b200_fp16_paged_decode")
+        if key is not None:
+            _runtime.fast_store(key, _runtime.FastEntry([(fn, args, _FP16_OUT_SLOT, "iris_b200_fp16_paged_decode")],
+                                                        device.index, stream, (ws, word)))
         if _runtime.validation_mode() == "sync":
             _runtime.raise_for_bits(_runtime.read_and_clear(word))
     return output

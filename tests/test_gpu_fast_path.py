@@ -80,3 +80,34 @@ def test_repeat_append_calls_are_bit_exact_and_still_validate():
                                      page_size=c["page_size"])
     for k, v in before.items():
         assert torch.equal(t[k], v)  # a rejected batch writes nothing
+
+
+def test_repeat_fp16_decode_calls_match_the_oracle_and_raise_device_errors():
+    from iris_kernel import _runtime
+    from iris_kernel.fused_attention import fused_fp16_paged_decode_attention
+
+    c = cases.decode_random_fp16(seed=93, B=3, Hq=16, Hkv=4, D=128, lens=[300, 5, 1200])
+    t = to_dev(c, cases.FP16_DECODE_KEYS)
+    args = [t[k] for k in cases.FP16_DECODE_KEYS]
+    ref = orc.decode_attention_fp16(*[c[k] for k in cases.FP16_DECODE_KEYS])
+    first = fused_fp16_paged_decode_attention(*args)
+    torch.cuda.synchronize()
+    assert_decode_close(first, ref)
+    out = torch.empty_like(first)
+    for _ in range(3):  # output given: the fast path after the first call
+        fused_fp16_paged_decode_attention(*args, out)
+        torch.cuda.synchronize()
+        assert torch.equal(out, first)
+    assert any(k[0] == "fp16_decode" for k in _runtime._fast)
+    assert torch.equal(fused_fp16_paged_decode_attention(*args), first)  # output allocated per call
+    with pytest.raises(ValueError):  # the cache's page size no longer matches
+        fused_fp16_paged_decode_attention(*args, page_size=32)
+    bt = t["block_table"]
+    good = bt[1, 0].item()
+    bt[1, 0] = t["k_cache"].shape[0] + 7  # same tensor, bad content: still caught on the device
+    with pytest.raises(IndexError):
+        fused_fp16_paged_decode_attention(*args, out)
+    bt[1, 0] = good
+    fused_fp16_paged_decode_attention(*args, out)
+    torch.cuda.synchronize()
+    assert torch.equal(out, first)
