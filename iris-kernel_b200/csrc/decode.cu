@@ -2243,6 +2243,11 @@ static int decode_entry(bool fp16, const void* query, const void* k_data, const 
     return IRIS_ECUDA;
   }
   int32_t max_ranges = max_ranges_for(qpk, num_kv_heads, device_sms(device), fp16);
+  // a batch holds at most batch * max_pages_per_seq pages, so the plan never
+  // cuts more ranges than problem_ranges: a small problem launches only the
+  // CTAs it can use (the range boundaries, and so the results, are the same)
+  const int32_t pcap = problem_ranges(batch, max_pages_per_seq);
+  if (pcap < max_ranges) max_ranges = pcap;
   if (ranges_limit > 0 && ranges_limit < max_ranges) max_ranges = ranges_limit;
   const Workspace ws = carve(workspace, batch, num_q_heads, head_dim, max_ranges);
   if (workspace_bytes < ws.bytes) return IRIS_EWORKSPACE;
