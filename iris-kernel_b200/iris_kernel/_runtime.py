@@ -20,6 +20,7 @@ the device and OR ``IRIS_ERR_*`` bits into an int32 error word:
 """
 from __future__ import annotations
 
+import ctypes
 import threading
 
 import torch
@@ -172,11 +173,20 @@ def workspace_bytes(fn, *shape) -> int:
 _FAST_MAX = 512
 
 
+def _prepared(fn, args):
+    """``fn`` as a bare function pointer plus ``args`` converted once to its
+    ctypes argument types: a repeat call then skips ctypes' per-argument
+    conversion (about 1.5 us of the ~3 us a 23-argument call costs)."""
+    bare = ctypes.CFUNCTYPE(fn.restype)(ctypes.cast(fn, ctypes.c_void_p).value)
+    return bare, [t(a) for t, a in zip(fn.argtypes, args)]
+
+
 class FastEntry:
     __slots__ = ("calls", "device", "stream", "keep")
 
     def __init__(self, calls, device, stream, keep):
-        self.calls = calls    # [(C function, argument list, output slot or -1, what)]
+        # [(bare C function, converted arguments, output slot or -1, what)]
+        self.calls = [(*_prepared(fn, args), slot, what) for fn, args, slot, what in calls]
         self.device = device  # CUDA device index
         self.stream = stream  # raw stream the arguments were prepared for
         self.keep = keep      # tensors the arguments point into (kept alive)
@@ -218,7 +228,7 @@ def fast_run(ent, out_ptr=None):
         for fn, args, slot, what in ent.calls:
             if slot >= 0:
                 args = list(args)
-                args[slot] = out_ptr
+                args[slot] = ctypes.c_void_p(out_ptr)
             _lib.check_status(fn(*args), what)
     finally:
         if cur != ent.device:
