@@ -2153,8 +2153,11 @@ cudaError_t launch_decode(const Plan& pl, const CUtensorMap& km, const CUtensorM
   }
   // programmatic launch: the combine CTAs are resident before the decode ends
   // lanes per output item: enough that each merges at most ~8 records in one
-  // load round (a sequence spans up to about ranges / batch + 2 ranges)
-  const int rec_est = ranges / p.batch + 2;
+  // load round (a sequence spans up to about ranges / batch + 2 ranges).  The
+  // estimate uses the device's range count, not the problem-capped grid: the
+  // lane count sets the merge order, so the output does not depend on the
+  // block table's width
+  const int rec_est = ls.ranges / p.batch + 2;
   int lanes = 1;
   while (lanes < 8 && (rec_est + lanes - 1) / lanes > 8) lanes <<= 1;
   p.combine_lanes = lanes;

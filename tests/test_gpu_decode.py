@@ -250,3 +250,18 @@ def test_config3_mha_varlen_sampled():
     seqs = [int(np.argmin(lens)), int(np.argmax(lens)), 5, 77]
     ref = torch_decode_fp32(q, kd, vd, ks, vs, bt, L, seqs=seqs)
     assert_decode_close(out[seqs], ref)
+
+
+@pytest.mark.parametrize("hq,hkv,d,lens", [(32, 8, 128, [300, 1200]), (16, 16, 64, [1, 17, 64]),
+                                           (64, 8, 128, [4096])])
+def test_grid_sized_by_the_block_table_width_gives_identical_results(hq, hkv, d, lens):
+    """The decode grid is capped by batch * block-table width / 4 ranges; the
+    ranges themselves depend only on the lengths, so a wide block table (the
+    full grid) and an exact one (a few CTAs) give bit-identical outputs."""
+    narrow = cases.decode_random(seed=hq + hkv + d + len(lens), B=len(lens), Hq=hq, Hkv=hkv, D=d, lens=lens)
+    wide = dict(narrow)
+    bt = narrow["block_table"]
+    wide["block_table"] = np.concatenate([bt, np.full((bt.shape[0], 3000), -1, np.int32)], axis=1)
+    a, b = _fused(narrow), _fused(wide)
+    assert torch.equal(a, b)
+    assert_decode_close(a, _oracle(narrow))
