@@ -56,15 +56,19 @@ cudaError_t clear_stale_cuda_error() { return cudaGetLastError(); }
 
 constexpr int kPage = 16;
 constexpr int kMinPagesPerRange = 4;  // ranges hold at least this many pages ...
-constexpr int kOnePageRanges = 32;    // ... unless the whole batch has at most this many pages
+constexpr int kOnePageRanges = 48;    // ... but one page when the batch has at most this many
+constexpr int kTwoPageRanges = 128;   // ... and two when it has at most this many
 
-// Page ranges a batch of U pages is cut into (before the grid's cap).  A
-// tiny batch (batch-1 decodes of up to 512 tokens) gets one page per range:
-// its CTAs then wait for one copy each instead of four in a row (decode of
-// 8 / 32 pages 10.4 -> 8.3 / 8.9 us); larger ones keep 4 pages per range, as
-// shorter ranges there cost more in the combine than they save.
+// Page ranges a batch of U pages is cut into (before the grid's cap).  Small
+// batches get shorter ranges, so their CTAs wait for one or two copies
+// instead of four in a row (batch-1 decode of 8 / 32 / 128 pages 10.4 / 10.4
+// / 12.4 -> 8.2 / 8.9 / 10.4 us); from 256 pages up shorter ranges cost more
+// in the combine than they save (256 pages after an L2 flush: 16.5 us at
+// four, 18.3 at two; 1024 pages: 14.5 us at four, 16.5 at two).
 __host__ __device__ __forceinline__ int64_t wanted_ranges(int64_t U) {
-  return U <= kOnePageRanges ? U : (U + kMinPagesPerRange - 1) / kMinPagesPerRange;
+  if (U <= kOnePageRanges) return U;
+  if (U <= kTwoPageRanges) return (U + 1) / 2;
+  return (U + kMinPagesPerRange - 1) / kMinPagesPerRange;
 }
 #define kNegInf (-__int_as_float(0x7f800000))
 
@@ -2191,13 +2195,15 @@ cudaError_t launch_decode(const Plan& pl, const CUtensorMap& km, const CUtensorM
 }  // namespace
 
 // Page ranges a problem can use at most: a batch holds at most
-// batch * max_pages_per_seq pages, and wanted_ranges(U) never exceeds
-// max(min(pages, kOnePageRanges), ceil(pages / kMinPagesPerRange)) for U <= pages.
+// batch * max_pages_per_seq pages, and for every U <= pages wanted_ranges(U)
+// is at most the largest of its three tiers' values at their largest U.
 int32_t problem_ranges(int32_t batch, int32_t max_pages_per_seq) {
   const int64_t pages = static_cast<int64_t>(batch) * (max_pages_per_seq > 0 ? max_pages_per_seq : 1);
-  const int64_t small = pages < kOnePageRanges ? pages : kOnePageRanges;
-  const int64_t big = (pages + kMinPagesPerRange - 1) / kMinPagesPerRange;
-  const int64_t r = small > big ? small : big;
+  const int64_t one = pages < kOnePageRanges ? pages : kOnePageRanges;
+  const int64_t two = ((pages < kTwoPageRanges ? pages : kTwoPageRanges) + 1) / 2;
+  const int64_t four = (pages + kMinPagesPerRange - 1) / kMinPagesPerRange;
+  int64_t r = one > two ? one : two;
+  r = r > four ? r : four;
   return static_cast<int32_t>(r < 1 ? 1 : (r > 0x7fffffff ? 0x7fffffff : r));
 }
 
