@@ -255,8 +255,9 @@ IRIS_API int iris_b200_fp16_paged_decode(const void* query, const void* k_cache,
  * that forbid allocation after start-up).
  *   - Nothing is allocated; returns IRIS_EWORKSPACE, before touching the
  *     array, when the problem needs more scratch than the array holds.  The
- *     need is sized by the problem: at most ceil(batch * max_pages_per_seq / 4)
- *     split-KV ranges (and never more than the GPU-wide maximum that
+ *     need is sized by the problem's pages P = batch * max_pages_per_seq: at
+ *     most max(min(P, 48), ceil(min(P, 128) / 2), ceil(P / 4)) split-KV
+ *     ranges (and never more than the GPU-wide maximum that
  *     iris_b200_decode_workspace_bytes assumes), each holding two records of
  *     num_q_heads * (head_dim + 1) floats.
  *   - The first call on a device looks up the array's device address
